@@ -1,0 +1,220 @@
+/*
+ * ltxb.h -- C ABI of libltxb.so, a B200-native (sm_100a) LTX-2.5 DiT block.
+ *
+ * The library replaces the reference's traced block executable
+ * (ABSatVPS/ltx-zml, ltx/block.zig) and its device upload path
+ * (ltx/loader.zig) behind a plain extern-C boundary: plain pointers and
+ * sizes, opaque handles, status codes. No torch or CUDA C++ types appear in
+ * the signatures; `stream` is a cudaStream_t passed as void*.
+ *
+ * Conventions
+ *  - Every function returns LTXB_OK (0) or a negative LTXB_E* code; the
+ *    message of the last failure on the calling thread is ltxb_last_error().
+ *    (The reference's boundary uses Zig error unions, ltx/loader.zig:63-128,
+ *    and the in-repo C-ABI precedent coli-zml/coli/abi.zig:1-10 returns
+ *    1/0; negative codes keep the error kind.)
+ *  - All device memory passed in is caller-owned and stream-ordered. Compute
+ *    entry points enqueue work on `stream` and return without a host sync;
+ *    device-side failures of bounded waits surface through
+ *    ltxb_device_status().
+ *  - Layouts are row-major. Activations are token-major [T, D] with D = H*128
+ *    and heads concatenated (head h occupies columns [128h, 128h+128)).
+ *  - Weights are [out, in] row-major as in the checkpoint; int8 weights carry
+ *    grouped-128 scales [out, in/128] (f32 as the reference stores them,
+ *    tools/quantize_block.py:70-73, or bf16 as the BASELINE configs ask).
+ */
+#ifndef LTXB_H
+#define LTXB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define LTXB_OK 0
+#define LTXB_EINVAL (-1)      /* bad argument / shape / alignment */
+#define LTXB_ECUDA (-2)       /* a CUDA runtime or driver call failed */
+#define LTXB_ENOMEM (-3)      /* device or host allocation failed */
+#define LTXB_ELAYOUT (-4)     /* blob layout: Misaligned / LayoutGap / TrailingBytes */
+#define LTXB_EMISSING (-5)    /* blob has no entry of a required name */
+#define LTXB_EDTYPE (-6)      /* blob entry has the wrong dtype or shape */
+#define LTXB_ENCCL (-7)       /* an NCCL call failed */
+#define LTXB_ETIMEOUT (-8)    /* a bounded device wait expired */
+#define LTXB_EUNSUPPORTED (-9)/* valid request this build does not implement */
+
+/* ---- enums ------------------------------------------------------------- */
+#define LTXB_DT_BF16 0
+#define LTXB_DT_F32 1
+#define LTXB_DT_I8 2
+
+/* Precision modes of a block (ltxb_weights_upload / ltxb_config.mode). */
+#define LTXB_MODE_F32 0   /* reference `Block`: bf16 weights upcast, f32 math     */
+#define LTXB_MODE_BF16 1  /* bf16 weights, bf16 activations on tcgen05, f32 accum */
+#define LTXB_MODE_INT8 2  /* reference `QBlock`: int8 g128 q/k/v (x2) + FFN       */
+
+/* Which linears LTXB_MODE_INT8 takes int8 (ltx/loader.zig:147-156 for the
+ * reference set; BASELINE config 3 also quantises the output projections). */
+#define LTXB_QSET_REF 0   /* q1,k1,v1,q2,k2,v2,ff1,ff2                           */
+#define LTXB_QSET_EXT 1   /* LTXB_QSET_REF + o1,o2                               */
+
+/* Stage selectors for ltxb_block_stage (ltx/block_conformance.zig:311-322). */
+#define LTXB_STAGE_S1_NORM_MSA 0
+#define LTXB_STAGE_S1B_QNORM 1
+#define LTXB_STAGE_S2_ATTN1_NOGATE 2
+#define LTXB_STAGE_S3_ATTN1 3
+#define LTXB_STAGE_S4_AFTER_SA 4
+#define LTXB_STAGE_S4_NORMED 5
+#define LTXB_STAGE_S5_CA_OUT 6
+#define LTXB_STAGE_S6_FF_IN 7
+#define LTXB_STAGE_S7_FF_OUT 8
+#define LTXB_STAGE_BLOCK_OUT 9
+
+/* ---- library ----------------------------------------------------------- */
+
+/* Initialise the library on one CUDA device (sets it current on the calling
+ * thread, resolves the TMA encoder). Replaces `Platform.auto`
+ * (ltx/e2e_prod.zig:187-189). Idempotent. */
+int ltxb_init(int device);
+
+/* Message for the last failure on the calling thread ("" if none). */
+const char* ltxb_last_error(void);
+
+/* Library version string. */
+const char* ltxb_version(void);
+
+/* Read (and, if clear != 0, reset) the device status word of the current
+ * device: LTXB_OK, or LTXB_ETIMEOUT when a kernel's bounded mbarrier/peer
+ * wait expired; *site (optional) receives the failing wait's site code.
+ * Synchronises the device. */
+int ltxb_device_status(int clear, uint32_t* site);
+
+/* ---- weights (ltx/loader.zig:133-172) ---------------------------------- */
+
+/* One entry of a packed block blob, in the format of tools/pack_block.py:
+ * `name` is the checkpoint name ("transformer_blocks.{i}.attn1.to_q.weight",
+ * companions "...::q8" / "...::q8scale"), matched after the reference's
+ * normalisation ('.' and '::' -> '_', ltx/loader.zig:102-129). */
+typedef struct {
+  const char* name;
+  int32_t dtype;       /* LTXB_DT_* */
+  int32_t ndim;        /* 1 or 2 */
+  int64_t shape[2];
+  uint64_t offset;     /* bytes from the blob start */
+  uint64_t nbytes;
+} ltxb_entry;
+
+typedef struct ltxb_weights ltxb_weights;
+
+/* Check the blob layout (ltx/loader.zig:73-82: 64-byte aligned offsets, gaps
+ * only alignment fill, no trailing bytes) without uploading anything.
+ * Returns LTXB_ELAYOUT with the reference's error name in the message. */
+int ltxb_blob_check_layout(const ltxb_entry* entries, int n_entries, uint64_t blob_bytes, uint32_t align);
+
+/* Upload one block's weights from a host blob into device-resident buffers
+ * on `device` (replaces buildBlockBufs + buildQuantBufs, ltx/loader.zig:
+ * 133-172). mode LTXB_MODE_F32/BF16 uploads the 28 base tensors; mode
+ * LTXB_MODE_INT8 uploads the int8/scale pairs of `qset` instead of those
+ * matrices' bf16 copies. `hidden` (D) and `ff` (FF) give the geometry
+ * (4096 / 16384 for LTX-2.5; D a multiple of 256, FF of 256). The device
+ * allocations are owned by the returned handle. Synchronous. */
+int ltxb_weights_upload(int device, const void* blob, uint64_t blob_bytes, const ltxb_entry* entries,
+                        int n_entries, int block_idx, int mode, int qset, int hidden, int ff,
+                        ltxb_weights** out);
+
+/* Device bytes held by a weights handle. */
+uint64_t ltxb_weights_bytes(const ltxb_weights* w);
+
+/* Free a weights handle (and its device buffers). NULL is a no-op. */
+void ltxb_weights_free(ltxb_weights* w);
+
+/* ---- sequence-parallel communicator ------------------------------------ */
+
+typedef struct ltxb_comm ltxb_comm;
+
+/* Size of the opaque unique id rank 0 creates and every rank receives. */
+int ltxb_comm_id_bytes(void);
+/* Rank 0: fill `id` (ltxb_comm_id_bytes() bytes). */
+int ltxb_comm_get_id(void* id);
+/* Every rank: join the group (NCCL over NVLink; one rank per GPU). */
+int ltxb_comm_init(const void* id, int rank, int nranks, int device, ltxb_comm** out);
+void ltxb_comm_free(ltxb_comm* c);
+
+/* ---- the block (ltx/block.zig:340-353, :544-574) ----------------------- */
+
+typedef struct {
+  int32_t T;          /* video tokens held by this rank (T_total / sp_size) */
+  int32_t S;          /* text (context) tokens                              */
+  int32_t K;          /* rows of the timestep table tstab                   */
+  int32_t mode;       /* LTXB_MODE_*; must match the weights' mode          */
+  int32_t sp_rank;    /* sequence-parallel rank (0 when sp_size == 1)       */
+  int32_t sp_size;    /* ranks sharing the T_total tokens                   */
+  ltxb_comm* comm;    /* required when sp_size > 1                          */
+} ltxb_config;
+
+/* Per-call tensors (device pointers). Shapes for one rank:
+ *   x, out   [T, D] f32   (out may alias x)
+ *   tstab    [K, 9, D] f32, tidx [T] int32   -- ada rows (ltx/block.zig:47-67)
+ *   ctx      [S, D] f32, pts2 [2, D] f32     -- cross-attention K/V modulation
+ *   cos, sin [T, H, 64] f32                  -- split-half RoPE tables
+ *   workspace: ltxb_block_workspace_bytes(cfg) bytes, 256-byte aligned. */
+typedef struct {
+  const float* x;
+  float* out;
+  const float* tstab;
+  const int32_t* tidx;
+  const float* ctx;
+  const float* pts2;
+  const float* cos;
+  const float* sin;
+  void* workspace;
+  uint64_t workspace_bytes;
+} ltxb_block_io;
+
+/* Workspace the block needs for `cfg` on weights `w`. */
+uint64_t ltxb_block_workspace_bytes(const ltxb_weights* w, const ltxb_config* cfg);
+
+/* out = block(x): the whole block, blockwise (flash) self-attention. The
+ * equivalent of exe.call on `wBlockOut` / `qBlockOutAll`
+ * (ltx/e2e_prod.zig:377-395). With sp_size > 1 the ranks exchange K/V
+ * shards over NVLink (ring attention); each rank holds its token slice. */
+int ltxb_block_forward(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_config* cfg, void* stream);
+
+/* One conformance stage (LTXB_STAGE_*) of the block, written to stage_out
+ * [T, D] f32 -- the staged methods s1NormMsa ... blockOut
+ * (ltx/block.zig:248-353, gated by ltx/block_conformance.zig:311-350).
+ * Single rank only. */
+int ltxb_block_stage(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_config* cfg, int stage,
+                     float* stage_out, void* stream);
+
+/* ---- standalone operators (BASELINE configs 1 and 2) ------------------- */
+
+/* Non-causal softmax attention, softmax(q k^T * scale) v, for H heads of
+ * 128 dims: q [Tq, H, 128], k/v [Tkv, H, 128], out [Tq, H, 128], all bf16
+ * (token-major, the block's layout). Blockwise online softmax (the
+ * reference's whileSdpa, ltx/block.zig:105-154; dense zml.nn.sdpa at
+ * ltx/block.zig:234 is the same function). `gate` (optional, f32 [Tq, H])
+ * multiplies each head's output (the block's 2*sigmoid gate). */
+int ltxb_attention(const void* q, const void* k, const void* v, void* out, const float* gate, int Tq, int Tkv,
+                   int H, float scale, void* stream);
+
+/* out[M, N] (bf16) = A[M, K] (bf16) . dequant(Wq[N, K] int8, scales[N, K/128])^T
+ * (+ bias[N] bf16, optional): the int8 grouped-128 dequant linear `linQ`
+ * (ltx/block.zig:462-477). scale_dtype LTXB_DT_F32 or LTXB_DT_BF16.
+ * fused != 0 dequantises tiles in shared memory inside the GEMM;
+ * fused == 0 expands the weights into `workspace` (N*K*2 bytes) with a
+ * bandwidth-bound pass and runs the bf16 GEMM. */
+int ltxb_dq_gemm(const void* A, const void* Wq, const void* scales, int scale_dtype, const void* bias, void* out,
+                 int M, int N, int K, int fused, void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* out[M, N] (bf16) = A[M, K] (bf16) . W[N, K] (bf16)^T (+ bias): the plain
+ * bf16 `lin` on tcgen05. */
+int ltxb_gemm_bf16(const void* A, const void* W, const void* bias, void* out, int M, int N, int K, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LTXB_H */

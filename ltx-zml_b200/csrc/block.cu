@@ -1,0 +1,747 @@
+// The LTX-2.5 DiT block behind the C ABI: device-resident weight upload from
+// the reference's blob format, workspace layout, and the launch sequence of
+// one block forward (ltx/block.zig:340-353 `wBlockOut`, :544-574
+// `qBlockOutAll`), single-GPU or sequence-parallel.
+//
+// Launch sequence (bf16 / int8 modes; f32 mode runs the same graph on the
+// SIMT f32 kernels):
+//   1  n    = rms(x) (1 + ada1) + ada0                      norm_modulate
+//   2  qkv  = n . [Wq;Wk;Wv]^T + b  (+ row sum-of-squares)   gemm  N = 3D
+//   3  gate = 2 sigmoid(n . Wg^T + bg)                       gemm  N = 32
+//   4  q,k  = rope(rms_w(q_raw)), rope(rms_w(k_raw))         qk_norm_rope2
+//   5  o    = softmax(q k^T / sqrt(128)) v * gate            attention (ring for SP)
+//   6  x_sa = x + (o . Wo^T + bo) * ada2                      gemm  (resid epilogue)
+//   7  a    = rms(x_sa) (1 + ada7) + ada6                     norm_modulate
+//   8  enc  = ctx (1 + kv1) + kv0;  [k2;v2] = enc . W^T + b    ctx_modulate + gemm (M = S)
+//   9  q2   = a . Wq2^T + b;  gate2                           gemm x2
+//  10  q2,k2 = rms_w(.)                                       qk_norm_rope (no RoPE)
+//  11  o2   = cross attention * gate2                          attention (T_kv = S)
+//  12  x_ca = x_sa + (o2 . Wo2^T + b) * ada8                  gemm
+//  13  f    = rms(x_ca) (1 + ada4) + ada3                      norm_modulate
+//  14  h    = gelu(f . W1^T)                                  gemm  N = FF
+//  15  out  = x_ca + (h . W2^T) * ada5                        gemm  K = FF
+#include <nccl.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ltxb {
+
+// ---------------------------------------------------------------------------
+// weights
+// ---------------------------------------------------------------------------
+struct Lin {
+  int N = 0, K = 0;
+  const void* w = nullptr;     // bf16 [N, K]
+  const int8_t* wq = nullptr;  // int8 [N, K]
+  const void* sc = nullptr;    // [N, K/128]
+  int sc_bf16 = 0;
+  const void* b = nullptr;     // bf16 [N] or null
+};
+
+}  // namespace ltxb
+
+struct ltxb_weights {
+  int device = 0, mode = 0, qset = 0, D = 0, FF = 0, H = 0, G = 0;
+  ltxb::Lin qkv1, g1, o1, q2, g2, kv2, o2, ff1, ff2;
+  const void *qn1 = nullptr, *kn1 = nullptr, *qn2 = nullptr, *kn2 = nullptr;
+  const float *sst = nullptr, *psst = nullptr;
+  std::vector<void*> allocs;
+  uint64_t bytes = 0;
+};
+
+struct ltxb_comm {
+  ncclComm_t nccl = nullptr;
+  int rank = 0, nranks = 1, device = 0;
+  cudaStream_t comm_stream = nullptr;
+  std::vector<cudaEvent_t> ev;  // pool of events for cross-stream ordering
+};
+
+namespace ltxb {
+
+static std::string norm_name(const char* n) {
+  std::string s;
+  for (const char* p = n; *p; ++p) {
+    if (p[0] == ':' && p[1] == ':') {
+      s.push_back('_');
+      ++p;
+    } else if (*p == '.') {
+      s.push_back('_');
+    } else {
+      s.push_back(*p);
+    }
+  }
+  return s;
+}
+
+struct Uploader {
+  ltxb_weights* w;
+  const uint8_t* blob;
+  uint64_t blob_bytes;
+  const ltxb_entry* e;
+  int n;
+  int block;
+
+  const ltxb_entry* find(const char* stem) {
+    char want[512];
+    snprintf(want, sizeof(want), "transformer_blocks_%d_%s", block, stem);
+    for (int i = 0; i < n; ++i)
+      if (norm_name(e[i].name) == want) return &e[i];
+    return nullptr;
+  }
+
+  int require(const char* stem, int dtype, int64_t r, int64_t c, const ltxb_entry** out) {
+    const ltxb_entry* x = find(stem);
+    if (!x) return set_error(LTXB_EMISSING, "blob %d: no entry named transformer_blocks_%d_%s", block, block, stem);
+    const int64_t cols = (x->ndim == 2) ? x->shape[1] : 1;
+    const int64_t rows = x->shape[0];
+    const bool shape_ok = (c == 0) ? (x->ndim == 1 && rows == r) : (x->ndim == 2 && rows == r && cols == c);
+    if (x->dtype != dtype || !shape_ok)
+      return set_error(LTXB_EDTYPE, "entry %s: dtype %d shape [%lld, %lld], expected dtype %d [%lld, %lld]", x->name,
+                       x->dtype, (long long)rows, (long long)cols, dtype, (long long)r, (long long)c);
+    const int esz = dtype == LTXB_DT_F32 ? 4 : dtype == LTXB_DT_BF16 ? 2 : 1;
+    const uint64_t need = (uint64_t)r * (c ? c : 1) * esz;
+    if (x->nbytes != need || x->offset + x->nbytes > blob_bytes)
+      return set_error(LTXB_ELAYOUT, "entry %s: %llu bytes at %llu does not fit (need %llu, blob %llu)", x->name,
+                       (unsigned long long)x->nbytes, (unsigned long long)x->offset, (unsigned long long)need,
+                       (unsigned long long)blob_bytes);
+    *out = x;
+    return LTXB_OK;
+  }
+
+  int alloc(size_t bytes, void** p) {
+    cudaError_t err = cudaMalloc(p, bytes < 256 ? 256 : bytes);
+    if (err != cudaSuccess) return set_error(LTXB_ENOMEM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(err));
+    w->allocs.push_back(*p);
+    w->bytes += bytes;
+    return LTXB_OK;
+  }
+
+  // copy `x` to dst + offset
+  int put(const ltxb_entry* x, void* dst, size_t off) {
+    cudaError_t err = cudaMemcpy(static_cast<uint8_t*>(dst) + off, blob + x->offset, x->nbytes, cudaMemcpyHostToDevice);
+    return err == cudaSuccess ? LTXB_OK : set_cuda_error(err, "weights H2D");
+  }
+
+  // one tensor, uploaded as is
+  int tensor(const char* stem, int dtype, int64_t r, int64_t c, const void** out) {
+    const ltxb_entry* x;
+    int rc = require(stem, dtype, r, c, &x);
+    if (rc) return rc;
+    void* p;
+    if ((rc = alloc(x->nbytes, &p))) return rc;
+    if ((rc = put(x, p, 0))) return rc;
+    *out = p;
+    return LTXB_OK;
+  }
+
+  // A linear made of 1..3 stacked checkpoint matrices [r_i, K] (bf16 or int8)
+  int linear(Lin& L, std::initializer_list<const char*> stems, int rows_each, int K, bool has_bias, bool quant,
+             int pad_rows = 0) {
+    const int parts = (int)stems.size();
+    const int N = parts * rows_each + pad_rows;
+    L.N = N;
+    L.K = K;
+    int rc;
+    if (quant) {
+      void *wq, *sc;
+      const ltxb_entry* first_sc = nullptr;
+      if ((rc = alloc((size_t)N * K, &wq))) return rc;
+      int i = 0;
+      for (const char* s : stems) {
+        char nm[256];
+        snprintf(nm, sizeof(nm), "%s_weight_q8", s);
+        const ltxb_entry* x;
+        if ((rc = require(nm, LTXB_DT_I8, rows_each, K, &x))) return rc;
+        if ((rc = put(x, wq, (size_t)i * rows_each * K))) return rc;
+        snprintf(nm, sizeof(nm), "%s_weight_q8scale", s);
+        const ltxb_entry* xs = find(nm);
+        if (!xs) return set_error(LTXB_EMISSING, "blob %d: no entry named transformer_blocks_%d_%s", block, block, nm);
+        if (!first_sc) {
+          first_sc = xs;
+          L.sc_bf16 = xs->dtype == LTXB_DT_BF16;
+          if ((rc = alloc((size_t)N * (K / 128) * (L.sc_bf16 ? 2 : 4), &sc))) return rc;
+        }
+        if ((rc = require(nm, L.sc_bf16 ? LTXB_DT_BF16 : LTXB_DT_F32, rows_each, K / 128, &xs))) return rc;
+        if ((rc = put(xs, sc, (size_t)i * rows_each * (K / 128) * (L.sc_bf16 ? 2 : 4)))) return rc;
+        ++i;
+      }
+      L.wq = static_cast<const int8_t*>(wq);
+      L.sc = sc;
+    } else {
+      void* wb;
+      if ((rc = alloc((size_t)N * K * 2, &wb))) return rc;
+      if (pad_rows && cudaMemset(wb, 0, (size_t)N * K * 2) != cudaSuccess)
+        return set_error(LTXB_ECUDA, "memset");
+      int i = 0;
+      for (const char* s : stems) {
+        char nm[256];
+        snprintf(nm, sizeof(nm), "%s_weight", s);
+        const ltxb_entry* x;
+        if ((rc = require(nm, LTXB_DT_BF16, rows_each, K, &x))) return rc;
+        if ((rc = put(x, wb, (size_t)i * rows_each * K * 2))) return rc;
+        ++i;
+      }
+      L.w = wb;
+    }
+    if (has_bias) {
+      void* bb;
+      if ((rc = alloc((size_t)N * 2, &bb))) return rc;
+      if (pad_rows && cudaMemset(bb, 0, (size_t)N * 2) != cudaSuccess) return set_error(LTXB_ECUDA, "memset");
+      int i = 0;
+      for (const char* s : stems) {
+        char nm[256];
+        snprintf(nm, sizeof(nm), "%s_bias", s);
+        const ltxb_entry* x;
+        if ((rc = require(nm, LTXB_DT_BF16, rows_each, 0, &x))) return rc;
+        if ((rc = put(x, bb, (size_t)i * rows_each * 2))) return rc;
+        ++i;
+      }
+      L.b = bb;
+    }
+    return LTXB_OK;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// workspace layout
+// ---------------------------------------------------------------------------
+struct Ws {
+  size_t off = 0;
+  uint8_t* base = nullptr;
+  template <class T>
+  T* take(size_t count, size_t elem = sizeof(T)) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * elem;
+    return p;
+  }
+};
+
+struct Bufs {
+  // activations: bf16 in tensor-core modes, f32 in f32 mode (`act` elem size)
+  void* n = nullptr;      // [T, D]   norm-modulate output (reused: attn_in, ff_in)
+  void* qkv = nullptr;    // [T, 3D]
+  float* ssq = nullptr;   // [T, 32]  q/k row sums of squares per N tile
+  void* q = nullptr;      // [T, D]
+  void* k = nullptr;      // [T_total, D]  (gathered for SP)
+  void* v = nullptr;      // [T_total, D]  (SP only)
+  float* gate = nullptr;  // [T, G]
+  void* o = nullptr;      // [T, D]   attention output (merged heads)
+  float* x_sa = nullptr;  // [T, D]
+  void* enc = nullptr;    // [S, D]
+  void* kv2 = nullptr;    // [S, 2D]
+  float* ssq2 = nullptr;  // [S, 32]
+  void* k2 = nullptr;     // [S, D]
+  float* x_ca = nullptr;  // [T, D]
+  void* h = nullptr;      // [T, FF]
+  void* deq = nullptr;    // [FF * D] bf16: int8 weights expanded (unfused int8 path)
+  float* o_acc = nullptr; // [T, D]  ring state
+  float* m_st = nullptr;  // [H, T]
+  float* l_st = nullptr;  // [H, T]
+};
+
+static bool g_fused_dequant = false;  // int8 GEMMs: dequantise in smem (true) or expand first (false)
+
+static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base, Bufs& b) {
+  Ws ws;
+  ws.base = base;
+  const size_t T = c->T, S = c->S, D = w->D, FF = w->FF;
+  const size_t Tt = (size_t)c->T * (c->sp_size > 1 ? c->sp_size : 1);
+  const size_t act = (w->mode == LTXB_MODE_F32) ? 4 : 2;
+  b.n = ws.take<uint8_t>(T * D, act);
+  b.qkv = ws.take<uint8_t>(T * 3 * D, act);
+  b.ssq = ws.take<float>(T * 32);
+  b.q = ws.take<uint8_t>(T * D, act);
+  b.k = ws.take<uint8_t>(Tt * D, act);
+  if (c->sp_size > 1) b.v = ws.take<uint8_t>(Tt * D, act);
+  b.gate = ws.take<float>(T * w->G);
+  b.o = ws.take<uint8_t>(T * D, act);
+  b.x_sa = ws.take<float>(T * D);
+  b.enc = ws.take<uint8_t>(S * D, act);
+  b.kv2 = ws.take<uint8_t>(S * 2 * D, act);
+  b.ssq2 = ws.take<float>(S * 32);
+  b.k2 = ws.take<uint8_t>(S * D, act);
+  b.x_ca = ws.take<float>(T * D);
+  b.h = ws.take<uint8_t>(T * FF, act);
+  if (w->mode == LTXB_MODE_INT8 && !g_fused_dequant) b.deq = ws.take<uint8_t>(FF * D, 2);
+  if (c->sp_size > 1) {
+    b.o_acc = ws.take<float>(T * D);
+    b.m_st = ws.take<float>((size_t)w->H * T);
+    b.l_st = ws.take<float>((size_t)w->H * T);
+  }
+  return (ws.off + 255) & ~size_t(255);
+}
+
+// ---------------------------------------------------------------------------
+// linears
+// ---------------------------------------------------------------------------
+struct LinCall {
+  const ltxb_weights* w;
+  Bufs* b;
+  cudaStream_t st;
+};
+
+// y = A . L^T with epilogue `epi`; tensor-core modes take bf16 A.
+static int run_lin(const LinCall& lc, const Lin& L, const void* A, int lda, int M, int epi, void* out, int ldo,
+                   float* ssq = nullptr, int ssq_cols = 0, const float* xres = nullptr, const float* tstab = nullptr,
+                   const int* tidx = nullptr, int ada_row = 0) {
+  const ltxb_weights* w = lc.w;
+  if (M <= 0) return LTXB_OK;
+  if (w->mode == LTXB_MODE_F32)
+    return gemm_f32(static_cast<const float*>(A), lda, L.w, M, L.N, L.K, L.b, epi, static_cast<float*>(out), ldo,
+                    ssq, 32, xres, w->sst, tstab, tidx, ada_row, lc.st);
+  GemmArgs g{};
+  g.A = A;
+  g.lda = lda;
+  g.M = M;
+  g.N = L.N;
+  g.K = L.K;
+  g.epi = epi;
+  g.bias = L.b;
+  g.out = out;
+  g.ldo = ldo;
+  g.ssq = ssq;
+  g.ssq_cols = ssq_cols;
+  g.ssq_ld = 32;
+  g.xres = xres;
+  g.ldx = ldo;
+  g.sst = w->sst;
+  g.tstab = tstab;
+  g.tidx = tidx;
+  g.ada_row = ada_row;
+  g.ada_d = w->D;
+  if (L.wq) {
+    if (g_fused_dequant) {
+      g.B = L.wq;
+      g.ldb = L.K;
+      g.b_int8 = 1;
+      g.scales = L.sc;
+      g.scale_bf16 = L.sc_bf16;
+    } else {
+      int rc = dequant_weights(L.wq, L.sc, L.sc_bf16, L.N, L.K, lc.b->deq, lc.st);
+      if (rc) return rc;
+      g.B = lc.b->deq;
+      g.ldb = L.K;
+    }
+  } else {
+    g.B = L.w;
+    g.ldb = L.K;
+  }
+  return gemm_tc(g, lc.st);
+}
+
+static int attn(const ltxb_weights* w, const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, void* out,
+                const float* gate, int Tq, int Tkv, cudaStream_t st) {
+  const float scale = 0.08838834764831845f;  // 1/sqrt(128)
+  if (w->mode == LTXB_MODE_F32)
+    return attention_f32(static_cast<const float*>(q), ldq, static_cast<const float*>(k), ldk,
+                         static_cast<const float*>(v), ldv, static_cast<float*>(out), gate, w->G, Tq, Tkv, w->H, scale,
+                         st);
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.ldq = ldq;
+  a.ldk = ldk;
+  a.ldv = ldv;
+  a.out = out;
+  a.gate = gate;
+  a.ldg = w->G;
+  a.Tq = Tq;
+  a.Tkv = Tkv;
+  a.H = w->H;
+  a.scale = scale;
+  return attention_tc(a, st);
+}
+
+// sequence-parallel self-attention: ring of K/V shards over NCCL, merging
+// (m, l, O) per shard; compute of shard s overlaps the receive of shard s+1.
+static int ring_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* v_local,
+                          int ldv_local, const float* gate, cudaStream_t st) {
+  ltxb_comm* cm = c->comm;
+  const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D;
+  const size_t chunk = (size_t)T * D * 2;
+  uint8_t* kb = static_cast<uint8_t*>(b.k);
+  uint8_t* vb = static_cast<uint8_t*>(b.v);
+  // local V into its slot of the gathered buffer (K was written there by qk-norm)
+  cudaError_t e = cudaMemcpy2DAsync(vb + (size_t)r * chunk, (size_t)D * 2, v_local, (size_t)ldv_local * 2,
+                                    (size_t)D * 2, T, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return set_cuda_error(e, "ring: local V copy");
+  if ((int)cm->ev.size() < 2 * N + 2) return set_error(LTXB_EINVAL, "ring: communicator event pool too small");
+  // comm stream starts after this rank's K/V are ready
+  cudaEventRecord(cm->ev[0], st);
+  cudaStreamWaitEvent(cm->comm_stream, cm->ev[0], 0);
+  const int next = (r + 1) % N, prev = (r - 1 + N) % N;
+  AttnArgs a{};
+  a.q = q;
+  a.ldq = D;
+  a.ldk = D;
+  a.ldv = D;
+  a.gate = gate;
+  a.ldg = w->G;
+  a.Tq = T;
+  a.Tkv = T;
+  a.H = w->H;
+  a.scale = 0.08838834764831845f;
+  a.o_acc = b.o_acc;
+  a.m_state = b.m_st;
+  a.l_state = b.l_st;
+  a.out = b.o;
+  for (int s = 0; s < N; ++s) {
+    const int cur = ((r - s) % N + N) % N;   // shard held at step s
+    const int nxt = ((r - s - 1) % N + N) % N;  // shard arriving during step s
+    if (s + 1 < N) {
+      ncclGroupStart();
+      ncclSend(kb + (size_t)cur * chunk, chunk, ncclUint8, next, cm->nccl, cm->comm_stream);
+      ncclRecv(kb + (size_t)nxt * chunk, chunk, ncclUint8, prev, cm->nccl, cm->comm_stream);
+      ncclSend(vb + (size_t)cur * chunk, chunk, ncclUint8, next, cm->nccl, cm->comm_stream);
+      ncclRecv(vb + (size_t)nxt * chunk, chunk, ncclUint8, prev, cm->nccl, cm->comm_stream);
+      ncclResult_t nr = ncclGroupEnd();
+      if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "ring step %d: %s", s, ncclGetErrorString(nr));
+      cudaEventRecord(cm->ev[1 + s], cm->comm_stream);
+    }
+    if (s > 0) cudaStreamWaitEvent(st, cm->ev[s], 0);  // shard `cur` has landed
+    a.k = kb + (size_t)cur * chunk;
+    a.v = vb + (size_t)cur * chunk;
+    a.first = (s == 0);
+    int rc = attention_tc(a, st);
+    if (rc) return rc;
+    // No other cross-stream edge is needed: every remote slot is received
+    // exactly once and before it is read, the local slot is never received
+    // into, and the send of step s+1 reads the slot the recv of step s wrote
+    // (same stream). The last compute step waits on the last group, so the
+    // comm stream is idle when the caller's stream is.
+  }
+  return attention_finalize(a, st);
+}
+
+// The block, up to `stage` (LTXB_STAGE_BLOCK_OUT = whole block).
+static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_config* c, int stage,
+                     float* stage_out, cudaStream_t st) {
+  if (!w || !io || !c) return set_error(LTXB_EINVAL, "null argument");
+  if (c->mode != w->mode) return set_error(LTXB_EINVAL, "config mode %d != weights mode %d", c->mode, w->mode);
+  if (c->T <= 0 || c->S <= 0 || c->K <= 0) return set_error(LTXB_EINVAL, "T, S and K must be positive");
+  const bool sp = c->sp_size > 1;
+  if (sp && (!c->comm || c->comm->nranks != c->sp_size || c->comm->rank != c->sp_rank))
+    return set_error(LTXB_EINVAL, "sp_size > 1 needs a communicator matching sp_rank/sp_size");
+  if (sp && w->mode == LTXB_MODE_F32) return set_error(LTXB_EUNSUPPORTED, "sequence parallelism runs bf16/int8 modes");
+  if (sp && stage != LTXB_STAGE_BLOCK_OUT) return set_error(LTXB_EINVAL, "stages are single-rank");
+  Bufs b;
+  const size_t need = layout(w, c, nullptr, b);
+  if (!io->workspace || io->workspace_bytes < need)
+    return set_error(LTXB_EINVAL, "workspace of %llu bytes is smaller than the %llu required",
+                     (unsigned long long)io->workspace_bytes, (unsigned long long)need);
+  if (reinterpret_cast<uintptr_t>(io->workspace) & 255) return set_error(LTXB_EINVAL, "workspace must be 256-byte aligned");
+  layout(w, c, static_cast<uint8_t*>(io->workspace), b);
+  const int T = c->T, S = c->S, D = w->D, FF = w->FF;
+  const bool f32 = w->mode == LTXB_MODE_F32;
+  const size_t act = f32 ? 4 : 2;
+  LinCall lc{w, &b, st};
+  int rc;
+#define CK(x)            \
+  do {                   \
+    if ((rc = (x))) return rc; \
+  } while (0)
+  auto col = [&](void* p, size_t c0) { return static_cast<void*>(static_cast<uint8_t*>(p) + c0 * act); };
+
+  // 1. n = modulate(rms(x), ada1, ada0)
+  if (stage == LTXB_STAGE_S1_NORM_MSA)
+    return norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, 0, 1, stage_out, 1, nullptr, st);
+  CK(norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, 0, 1, b.n, f32, nullptr, st));
+  // 2. fused q/k/v projection (+ q/k sums of squares)
+  CK(run_lin(lc, w->qkv1, b.n, D, T, f32 ? EPI_F32 : EPI_BF16_SSQ, b.qkv, 3 * D, b.ssq, 2 * D));
+  const int n_ssq = D / 256;  // N tiles per q (or k) part at BN = 256
+  if (stage == LTXB_STAGE_S1B_QNORM) {
+    if (f32) return qk_norm_rope_f32(static_cast<const float*>(b.qkv), 3 * D, w->qn1, nullptr, nullptr, T, D, stage_out, st);
+    return qk_norm_rope(b.qkv, 3 * D, b.ssq, 32, n_ssq, w->qn1, nullptr, nullptr, T, D, nullptr, stage_out, st);
+  }
+  // 3. gate logits
+  const bool gated = stage != LTXB_STAGE_S2_ATTN1_NOGATE;
+  if (gated) CK(run_lin(lc, w->g1, b.n, D, T, EPI_GATE2SIG_F32, b.gate, w->G));
+  // 4. q/k norm + RoPE (K goes to its slot of the gathered buffer under SP)
+  void* k_dst = col(b.k, (size_t)(sp ? c->sp_rank : 0) * T * D);
+  if (f32) {
+    CK(qk_norm_rope_f32(static_cast<const float*>(b.qkv), 3 * D, w->qn1, io->cos, io->sin, T, D,
+                        static_cast<float*>(b.q), st));
+    CK(qk_norm_rope_f32(static_cast<const float*>(b.qkv) + D, 3 * D, w->kn1, io->cos, io->sin, T, D,
+                        static_cast<float*>(k_dst), st));
+  } else {
+    CK(qk_norm_rope2(b.qkv, col(b.qkv, D), 3 * D, b.ssq, b.ssq + n_ssq, 32, n_ssq, w->qn1, w->kn1, io->cos, io->sin,
+                     T, D, b.q, k_dst, st));
+  }
+  // 5. self-attention
+  const float* g1 = gated ? b.gate : nullptr;
+  if (sp)
+    CK(ring_attention(w, c, b, b.q, col(b.qkv, 2 * D), 3 * D, g1, st));
+  else
+    CK(attn(w, b.q, D, b.k, D, col(b.qkv, 2 * D), 3 * D, b.o, g1, T, T, st));
+  if (stage == LTXB_STAGE_S2_ATTN1_NOGATE || stage == LTXB_STAGE_S3_ATTN1)
+    return run_lin(lc, w->o1, b.o, D, T, EPI_F32, stage_out, D);
+  // 6. x_sa = x + (o Wo^T + bo) * ada2
+  CK(run_lin(lc, w->o1, b.o, D, T, EPI_RESID_F32, b.x_sa, D, nullptr, 0, io->x, io->tstab, io->tidx, 2));
+  if (stage == LTXB_STAGE_S4_AFTER_SA)
+    return cudaMemcpyAsync(stage_out, b.x_sa, (size_t)T * D * 4, cudaMemcpyDeviceToDevice, st) == cudaSuccess
+               ? LTXB_OK
+               : set_error(LTXB_ECUDA, "stage copy");
+  if (stage == LTXB_STAGE_S4_NORMED) return rms_rows(b.x_sa, T, D, stage_out, st);
+  // 7. cross-attention query input
+  CK(norm_modulate(b.x_sa, T, D, w->sst, io->tstab, io->tidx, 6, 7, b.n, f32, nullptr, st));
+  // 8. prompt K/V
+  CK(ctx_modulate(io->ctx, S, D, w->psst, io->pts2, f32 ? nullptr : b.enc, f32 ? static_cast<float*>(b.enc) : nullptr,
+                  st));
+  CK(run_lin(lc, w->kv2, b.enc, D, S, f32 ? EPI_F32 : EPI_BF16_SSQ, b.kv2, 2 * D, b.ssq2, D));
+  // 9. q2 and gate2
+  CK(run_lin(lc, w->q2, b.n, D, T, f32 ? EPI_F32 : EPI_BF16_SSQ, b.qkv, D, b.ssq, D));
+  CK(run_lin(lc, w->g2, b.n, D, T, EPI_GATE2SIG_F32, b.gate, w->G));
+  // 10. q2 / k2 norms (no RoPE in cross-attention, ltx/block.zig:304)
+  if (f32) {
+    CK(qk_norm_rope_f32(static_cast<const float*>(b.qkv), D, w->qn2, nullptr, nullptr, T, D, static_cast<float*>(b.q), st));
+    CK(qk_norm_rope_f32(static_cast<const float*>(b.kv2), 2 * D, w->kn2, nullptr, nullptr, S, D,
+                        static_cast<float*>(b.k2), st));
+  } else {
+    CK(qk_norm_rope(b.qkv, D, b.ssq, 32, n_ssq, w->qn2, nullptr, nullptr, T, D, b.q, nullptr, st));
+    CK(qk_norm_rope(b.kv2, 2 * D, b.ssq2, 32, n_ssq, w->kn2, nullptr, nullptr, S, D, b.k2, nullptr, st));
+  }
+  // 11. cross-attention
+  CK(attn(w, b.q, D, b.k2, D, col(b.kv2, D), 2 * D, b.o, b.gate, T, S, st));
+  // 12. x_ca = x_sa + (o2 Wo2^T + b) * ada8
+  if (stage == LTXB_STAGE_S5_CA_OUT)
+    return run_lin(lc, w->o2, b.o, D, T, EPI_RESID_F32, stage_out, D, nullptr, 0, nullptr, io->tstab, io->tidx, 8);
+  CK(run_lin(lc, w->o2, b.o, D, T, EPI_RESID_F32, b.x_ca, D, nullptr, 0, b.x_sa, io->tstab, io->tidx, 8));
+  // 13. FFN input
+  if (stage == LTXB_STAGE_S6_FF_IN)
+    return norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, 3, 4, stage_out, 1, nullptr, st);
+  CK(norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, 3, 4, b.n, f32, nullptr, st));
+  // 14. h = gelu(f W1^T)
+  CK(run_lin(lc, w->ff1, b.n, D, T, EPI_GELU_BF16, b.h, FF));
+  // 15. out = x_ca + (h W2^T) * ada5
+  if (stage == LTXB_STAGE_S7_FF_OUT) return run_lin(lc, w->ff2, b.h, FF, T, EPI_F32, stage_out, D);
+  CK(run_lin(lc, w->ff2, b.h, FF, T, EPI_RESID_F32, io->out, D, nullptr, 0, b.x_ca, io->tstab, io->tidx, 5));
+#undef CK
+  return LTXB_OK;
+}
+
+}  // namespace ltxb
+
+using namespace ltxb;
+
+extern "C" {
+
+int ltxb_blob_check_layout(const ltxb_entry* entries, int n_entries, uint64_t blob_bytes, uint32_t align) {
+  if (n_entries < 0 || (n_entries > 0 && !entries) || align == 0) return set_error(LTXB_EINVAL, "bad arguments");
+  uint64_t end = 0;
+  for (int i = 0; i < n_entries; ++i) {
+    const ltxb_entry& e = entries[i];
+    if (e.offset % align) return set_error(LTXB_ELAYOUT, "Misaligned: %s at %llu", e.name, (unsigned long long)e.offset);
+    if (e.offset < end || e.offset - end >= align)
+      return set_error(LTXB_ELAYOUT, "LayoutGap: %s at %llu after %llu", e.name, (unsigned long long)e.offset,
+                       (unsigned long long)end);
+    end = e.offset + e.nbytes;
+  }
+  if (end != blob_bytes)
+    return set_error(LTXB_ELAYOUT, "TrailingBytes: entries end at %llu, blob is %llu", (unsigned long long)end,
+                     (unsigned long long)blob_bytes);
+  return LTXB_OK;
+}
+
+void ltxb_weights_free(ltxb_weights* w) {
+  if (!w) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(w->device);
+  for (void* p : w->allocs) cudaFree(p);
+  cudaSetDevice(prev);
+  delete w;
+}
+
+uint64_t ltxb_weights_bytes(const ltxb_weights* w) { return w ? w->bytes : 0; }
+
+int ltxb_weights_upload(int device, const void* blob, uint64_t blob_bytes, const ltxb_entry* entries, int n_entries,
+                        int block_idx, int mode, int qset, int hidden, int ff, ltxb_weights** out) {
+  if (!out) return set_error(LTXB_EINVAL, "out is null");
+  *out = nullptr;
+  if (!blob || !entries || n_entries <= 0) return set_error(LTXB_EINVAL, "empty blob");
+  if (mode < LTXB_MODE_F32 || mode > LTXB_MODE_INT8) return set_error(LTXB_EINVAL, "unknown mode %d", mode);
+  if (hidden <= 0 || hidden % 256 || ff <= 0 || ff % 256)
+    return set_error(LTXB_EINVAL, "hidden (%d) and ff (%d) must be positive multiples of 256", hidden, ff);
+  int rc = ltxb_init(device);
+  if (rc) return rc;
+  auto* w = new ltxb_weights();
+  w->device = device;
+  w->mode = mode;
+  w->qset = qset;
+  w->D = hidden;
+  w->FF = ff;
+  w->H = hidden / 128;
+  w->G = (w->H + 31) / 32 * 32;
+  Uploader u{w, static_cast<const uint8_t*>(blob), blob_bytes, entries, n_entries, block_idx};
+  const int D = hidden, H = w->H;
+  const bool q8 = mode == LTXB_MODE_INT8;
+  const bool qo = q8 && qset == LTXB_QSET_EXT;
+  rc = u.linear(w->qkv1, {"attn1_to_q", "attn1_to_k", "attn1_to_v"}, D, D, true, q8);
+  if (!rc) rc = u.linear(w->g1, {"attn1_to_gate_logits"}, H, D, true, false, w->G - H);
+  if (!rc) rc = u.linear(w->o1, {"attn1_to_out_0"}, D, D, true, qo);
+  if (!rc) rc = u.linear(w->q2, {"attn2_to_q"}, D, D, true, q8);
+  if (!rc) rc = u.linear(w->g2, {"attn2_to_gate_logits"}, H, D, true, false, w->G - H);
+  if (!rc) rc = u.linear(w->kv2, {"attn2_to_k", "attn2_to_v"}, D, D, true, q8);
+  if (!rc) rc = u.linear(w->o2, {"attn2_to_out_0"}, D, D, true, qo);
+  if (!rc) rc = u.linear(w->ff1, {"ff_net_0_proj"}, ff, D, false, q8);
+  if (!rc) rc = u.linear(w->ff2, {"ff_net_2"}, D, ff, false, q8);
+  if (!rc) rc = u.tensor("attn1_q_norm_weight", LTXB_DT_BF16, D, 0, &w->qn1);
+  if (!rc) rc = u.tensor("attn1_k_norm_weight", LTXB_DT_BF16, D, 0, &w->kn1);
+  if (!rc) rc = u.tensor("attn2_q_norm_weight", LTXB_DT_BF16, D, 0, &w->qn2);
+  if (!rc) rc = u.tensor("attn2_k_norm_weight", LTXB_DT_BF16, D, 0, &w->kn2);
+  const void *sst = nullptr, *psst = nullptr;
+  if (!rc) rc = u.tensor("scale_shift_table", LTXB_DT_F32, 9, D, &sst);
+  if (!rc) rc = u.tensor("prompt_scale_shift_table", LTXB_DT_F32, 2, D, &psst);
+  if (rc) {
+    ltxb_weights_free(w);
+    return rc;
+  }
+  w->sst = static_cast<const float*>(sst);
+  w->psst = static_cast<const float*>(psst);
+  *out = w;
+  return LTXB_OK;
+}
+
+uint64_t ltxb_block_workspace_bytes(const ltxb_weights* w, const ltxb_config* cfg) {
+  if (!w || !cfg) return 0;
+  Bufs b;
+  return layout(w, cfg, nullptr, b);
+}
+
+int ltxb_block_forward(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_config* cfg, void* stream) {
+  return run_block(w, io, cfg, LTXB_STAGE_BLOCK_OUT, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int ltxb_block_stage(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_config* cfg, int stage,
+                     float* stage_out, void* stream) {
+  if (stage < 0 || stage > LTXB_STAGE_BLOCK_OUT) return set_error(LTXB_EINVAL, "unknown stage %d", stage);
+  if (stage != LTXB_STAGE_BLOCK_OUT && !stage_out) return set_error(LTXB_EINVAL, "stage_out is null");
+  if (stage == LTXB_STAGE_BLOCK_OUT) {
+    int rc = run_block(w, io, cfg, stage, nullptr, static_cast<cudaStream_t>(stream));
+    if (rc || !stage_out || stage_out == io->out) return rc;
+    cudaError_t e = cudaMemcpyAsync(stage_out, io->out, (size_t)cfg->T * w->D * 4, cudaMemcpyDeviceToDevice,
+                                    static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "stage copy");
+  }
+  return run_block(w, io, cfg, stage, stage_out, static_cast<cudaStream_t>(stream));
+}
+
+// ---- communicator ----
+int ltxb_comm_id_bytes(void) { return (int)sizeof(ncclUniqueId); }
+
+int ltxb_comm_get_id(void* id) {
+  if (!id) return set_error(LTXB_EINVAL, "id is null");
+  ncclResult_t r = ncclGetUniqueId(static_cast<ncclUniqueId*>(id));
+  return r == ncclSuccess ? LTXB_OK : set_error(LTXB_ENCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+}
+
+int ltxb_comm_init(const void* id, int rank, int nranks, int device, ltxb_comm** out) {
+  if (!id || !out || nranks < 1 || rank < 0 || rank >= nranks) return set_error(LTXB_EINVAL, "bad communicator args");
+  *out = nullptr;
+  int rc = ltxb_init(device);
+  if (rc) return rc;
+  auto* c = new ltxb_comm();
+  c->rank = rank;
+  c->nranks = nranks;
+  c->device = device;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclResult_t r = ncclCommInitRank(&c->nccl, nranks, uid, rank);
+  if (r != ncclSuccess) {
+    delete c;
+    return set_error(LTXB_ENCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+  }
+  if (cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    ncclCommDestroy(c->nccl);
+    delete c;
+    return set_error(LTXB_ECUDA, "comm stream");
+  }
+  c->ev.resize(2 * nranks + 2);
+  for (auto& e : c->ev) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+  *out = c;
+  return LTXB_OK;
+}
+
+void ltxb_comm_free(ltxb_comm* c) {
+  if (!c) return;
+  if (c->comm_stream) cudaStreamSynchronize(c->comm_stream);
+  for (auto& e : c->ev) cudaEventDestroy(e);
+  if (c->nccl) ncclCommDestroy(c->nccl);
+  if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
+  delete c;
+}
+
+// ---- standalone operators ----
+int ltxb_attention(const void* q, const void* k, const void* v, void* out, const float* gate, int Tq, int Tkv, int H,
+                   float scale, void* stream) {
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.ldq = a.ldk = a.ldv = H * 128;
+  a.out = out;
+  a.gate = gate;
+  a.ldg = H;
+  a.Tq = Tq;
+  a.Tkv = Tkv;
+  a.H = H;
+  a.scale = scale;
+  return attention_tc(a, static_cast<cudaStream_t>(stream));
+}
+
+int ltxb_dq_gemm(const void* A, const void* Wq, const void* scales, int scale_dtype, const void* bias, void* out, int M,
+                 int N, int K, int fused, void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (scale_dtype != LTXB_DT_F32 && scale_dtype != LTXB_DT_BF16) return set_error(LTXB_EINVAL, "scale dtype");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GemmArgs g{};
+  g.A = A;
+  g.lda = K;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epi = EPI_BF16;
+  g.bias = bias;
+  g.out = out;
+  g.ldo = N;
+  if (fused) {
+    g.B = Wq;
+    g.ldb = K;
+    g.b_int8 = 1;
+    g.scales = scales;
+    g.scale_bf16 = scale_dtype == LTXB_DT_BF16;
+  } else {
+    if (!workspace || workspace_bytes < (uint64_t)N * K * 2)
+      return set_error(LTXB_EINVAL, "dq_gemm: unfused path needs N*K*2 workspace bytes");
+    int rc = dequant_weights(static_cast<const int8_t*>(Wq), scales, scale_dtype == LTXB_DT_BF16, N, K, workspace, st);
+    if (rc) return rc;
+    g.B = workspace;
+    g.ldb = K;
+  }
+  return gemm_tc(g, st);
+}
+
+int ltxb_gemm_bf16(const void* A, const void* W, const void* bias, void* out, int M, int N, int K, void* stream) {
+  GemmArgs g{};
+  g.A = A;
+  g.lda = K;
+  g.B = W;
+  g.ldb = K;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epi = EPI_BF16;
+  g.bias = bias;
+  g.out = out;
+  g.ldo = N;
+  return gemm_tc(g, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,386 @@
+// tcgen05 GEMM for the block's linears: D[M, N] = A[M, K] . B[N, K]^T with
+// bf16 A (activations, token-major) and B either bf16 or int8 + grouped-128
+// scales (weights, [out, in] row-major as stored in the checkpoint), f32
+// accumulation in TMEM, and the block's elementwise tails fused into the
+// epilogue (bias, q/k-norm sum of squares, GELU, 2*sigmoid gate, gated f32
+// residual).
+//
+// Replaces the reference's `lin` / `linQ` (ltx/block.zig:22-26, :462-477),
+// which upcast the weights to f32 per call and run f32 dots.
+//
+// Structure (one CTA per SM, persistent over output tiles 128 x BN):
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per stage
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, fused tail, stores
+//   warps 6..9  (int8 B only) dequantisers: int8 tile + per-group scale ->
+//               bf16 tile in the 128B-swizzled K-major layout the MMA reads
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
+// the main loop of tile i+1.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ltxb {
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_GROUP_M = 16;  // M tiles walked together for L2 reuse
+
+template <int BN, bool BQ8>
+struct GemmCfg {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;   // 16 KB
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;        // bf16 tile
+  static constexpr int BQ_BYTES = BQ8 ? BN * GEMM_BK : 0; // int8 tile
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + BQ_BYTES;
+  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int NUM_THREADS = BQ8 ? 320 : 192;
+  static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
+  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns must be a power of two");
+};
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), hardware tanh approximation
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  float u = k0 * fmaf(k1 * x, x * x, x);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * x * (1.0f + t);
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& m, int& n) {
+  const int per_group = GEMM_GROUP_M * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * GEMM_GROUP_M;
+  const int gm = min(GEMM_GROUP_M, num_m - first_m);
+  const int idx = tile - g * per_group;
+  m = first_m + idx % gm;
+  n = idx / gm;
+}
+
+// int8 x 8 -> bf16 x 8 with one scale: x in [-128, 127] is rebuilt exactly as
+// a float from the magic constant 2^23 (0x4B000000 | (x + 128)) minus
+// (2^23 + 128), scaled in f32 and rounded once to bf16.
+__device__ __forceinline__ uint4 dequant8(uint2 q, float s) {
+  const uint32_t w0 = q.x ^ 0x80808080u, w1 = q.y ^ 0x80808080u;
+  const float bias = 8388736.0f;  // 2^23 + 128
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t b0, b1;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(b0) : "r"(w0), "r"(0x4B000000u), "r"(0x7650u | (uint32_t)i));
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(b1) : "r"(w1), "r"(0x4B000000u), "r"(0x7650u | (uint32_t)i));
+    f[i] = (__uint_as_float(b0) - bias) * s;
+    f[4 + i] = (__uint_as_float(b1) - bias) * s;
+  }
+  uint4 o;
+  o.x = pack_bf16x2(f[0], f[1]);
+  o.y = pack_bf16x2(f[2], f[3]);
+  o.z = pack_bf16x2(f[4], f[5]);
+  o.w = pack_bf16x2(f[6], f[7]);
+  return o;
+}
+
+template <int BN, bool BQ8, int EPI>
+__global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  using C = GemmCfg<BN, BQ8>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + S * C::A_BYTES;
+  uint8_t* sBq = sB + S * C::B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sBq + S * C::BQ_BYTES);
+  uint64_t* full = bars;            // TMA -> (dequant | MMA)
+  uint64_t* deq = bars + S;         // dequant -> MMA
+  uint64_t* empty = bars + 2 * S;   // MMA -> TMA
+  uint64_t* tfull = bars + 3 * S;   // MMA -> epilogue, 2 accumulators
+  uint64_t* tempty = tfull + 2;     // epilogue -> MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int M = args.M, N = args.N, K = args.K;
+  const int num_m = (M + GEMM_BM - 1) / GEMM_BM, num_n = N / BN, nkb = K / GEMM_BK;
+  const int num_tiles = num_m * num_n;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&deq[i], 4);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      const uint32_t bytes = C::A_BYTES + (BQ8 ? C::BQ_BYTES : C::B_BYTES);
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int m, n;
+        tile_coords(tile, num_m, num_n, m, n);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, 0x101)) goto done;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * GEMM_BK, m * GEMM_BM);
+          if (BQ8)
+            tma_load_2d(sBq + s * C::BQ_BYTES, &tmB, &full[s], kb * GEMM_BK, n * BN);
+          else
+            tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * GEMM_BK, n * BN);
+          if (++s == S) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], aph ^ 1, 0x102)) goto done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(BQ8 ? &deq[s] : &full[s], ph, 0x103)) goto done;
+          tc_fence_after();
+          const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + s * C::A_BYTES));
+          const uint64_t db = sdesc_kmajor_sw128(smem_u32(sB + s * C::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k)
+            umma_ss(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&empty[s]);
+          if (++s == S) { s = 0; ph ^= 1; }
+        }
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_local = q * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      int m, n;
+      tile_coords(tile, num_m, num_n, m, n);
+      const int acc = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      if (!warp_wait(&tfull[acc], aph, 0x104)) break;
+      tc_fence_after();
+      const int row = m * GEMM_BM + row_local;
+      const bool row_ok = row < M;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      float ssq = 0.f;
+      int trow = 0;
+      if (EPI == EPI_RESID_F32 && row_ok) trow = args.tidx[row];
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tbase + cc * 32, r);
+        tmem_wait_ld();
+        const int col0 = n * BN + cc * 32;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (args.bias != nullptr) {
+          const uint4* bp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(args.bias) + col0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 b = __ldg(bp + j);
+            v[8 * j + 0] += bf16_lo(b.x); v[8 * j + 1] += bf16_hi(b.x);
+            v[8 * j + 2] += bf16_lo(b.y); v[8 * j + 3] += bf16_hi(b.y);
+            v[8 * j + 4] += bf16_lo(b.z); v[8 * j + 5] += bf16_hi(b.z);
+            v[8 * j + 6] += bf16_lo(b.w); v[8 * j + 7] += bf16_hi(b.w);
+          }
+        }
+        if (!row_ok) continue;
+        if (EPI == EPI_BF16 || EPI == EPI_BF16_SSQ || EPI == EPI_GELU_BF16) {
+          if (EPI == EPI_GELU_BF16) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
+          }
+          if (EPI == EPI_BF16_SSQ) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ssq = fmaf(v[j], v[j], ssq);
+          }
+          uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) +
+                                               (size_t)row * args.ldo + col0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 o;
+            o.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            o.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            o.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            o.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            op[j] = o;
+          }
+        } else if (EPI == EPI_RESID_F32) {
+          // out = xres + y * (sst[r] + tstab[tidx[row], r])
+          const float4* xp =
+              args.xres ? reinterpret_cast<const float4*>(args.xres + (size_t)row * args.ldx + col0) : nullptr;
+          const float4* sp = reinterpret_cast<const float4*>(args.sst + (size_t)args.ada_row * args.ada_d + col0);
+          const float4* tp = reinterpret_cast<const float4*>(
+              args.tstab + ((size_t)trow * 9 + args.ada_row) * args.ada_d + col0);
+          float4* op = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + col0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 xv = xp ? xp[j] : make_float4(0.f, 0.f, 0.f, 0.f), sv = __ldg(sp + j), tv = __ldg(tp + j), o;
+            o.x = xv.x + v[4 * j + 0] * (tv.x + sv.x);
+            o.y = xv.y + v[4 * j + 1] * (tv.y + sv.y);
+            o.z = xv.z + v[4 * j + 2] * (tv.z + sv.z);
+            o.w = xv.w + v[4 * j + 3] * (tv.w + sv.w);
+            op[j] = o;
+          }
+        } else {  // EPI_F32 / EPI_GATE2SIG_F32
+          float4* op = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + col0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            if (EPI == EPI_GATE2SIG_F32) {
+              o.x = 2.0f / (1.0f + __expf(-o.x));
+              o.y = 2.0f / (1.0f + __expf(-o.y));
+              o.z = 2.0f / (1.0f + __expf(-o.z));
+              o.w = 2.0f / (1.0f + __expf(-o.w));
+            }
+            op[j] = o;
+          }
+        }
+      }
+      if (EPI == EPI_BF16_SSQ && row_ok && n * BN < args.ssq_cols)
+        args.ssq[(size_t)row * args.ssq_ld + n] = ssq;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  } else if (BQ8) {
+    // ---------------- dequantisers (warps 6..9) ----------------
+    const int td = threadIdx.x - 192;  // 0..127
+    int s = 0;
+    uint32_t ph = 0;
+    const int ngroups = K / 128;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int m, n;
+      tile_coords(tile, num_m, num_n, m, n);
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!warp_wait(&full[s], ph, 0x105)) goto done;
+        const uint8_t* src = sBq + s * C::BQ_BYTES;
+        uint8_t* dst = sB + s * C::B_BYTES;
+        const int g = (kb * GEMM_BK) >> 7;
+#pragma unroll 4
+        for (int j = 0; j < BN * 8 / 128; ++j) {
+          const int id = j * 128 + td;
+          const int r = id >> 3, c = id & 7;
+          const size_t si = (size_t)(n * BN + r) * ngroups + g;
+          const float sc = args.scale_bf16
+                               ? __uint_as_float((uint32_t)__ldg(reinterpret_cast<const uint16_t*>(args.scales) + si) << 16)
+                               : __ldg(reinterpret_cast<const float*>(args.scales) + si);
+          const uint2 qv = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
+          *reinterpret_cast<uint4*>(dst + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = dequant8(qv, sc);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&deq[s]);
+        if (++s == S) { s = 0; ph ^= 1; }
+      }
+    }
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+template <int BN, bool BQ8, int EPI>
+static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+  using C = GemmCfg<BN, BQ8>;
+  auto kern = gemm_tc_kernel<BN, BQ8, EPI>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return set_cuda_error(e, "gemm: cudaFuncSetAttribute");
+    attr_set[dev & 63] = true;
+  }
+  const int num_tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * (a.N / BN);
+  const int grid = num_tiles < sm_count() ? num_tiles : sm_count();
+  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "gemm launch");
+  return LTXB_OK;
+}
+
+template <int BN, bool BQ8>
+static int dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+  switch (a.epi) {
+    case EPI_BF16: return launch_one<BN, BQ8, EPI_BF16>(ta, tb, a, st);
+    case EPI_BF16_SSQ: return launch_one<BN, BQ8, EPI_BF16_SSQ>(ta, tb, a, st);
+    case EPI_GELU_BF16: return launch_one<BN, BQ8, EPI_GELU_BF16>(ta, tb, a, st);
+    case EPI_RESID_F32: return launch_one<BN, BQ8, EPI_RESID_F32>(ta, tb, a, st);
+    case EPI_GATE2SIG_F32: return launch_one<BN, BQ8, EPI_GATE2SIG_F32>(ta, tb, a, st);
+    case EPI_F32: return launch_one<BN, BQ8, EPI_F32>(ta, tb, a, st);
+  }
+  return set_error(LTXB_EINVAL, "gemm: unknown epilogue");
+}
+
+int gemm_tc(const GemmArgs& a, cudaStream_t st) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return set_error(LTXB_EINVAL, "gemm: empty shape");
+  if (a.K % GEMM_BK) return set_error(LTXB_EINVAL, "gemm: K must be a multiple of 64");
+  if (a.b_int8 && (a.K % 128)) return set_error(LTXB_EINVAL, "gemm: int8 weights need K % 128 == 0");
+  int bn = a.bn;
+  if (bn == 0) bn = (a.N % 256 == 0) ? 256 : (a.N % 128 == 0) ? 128 : (a.N % 32 == 0 ? 32 : 0);
+  if (bn == 0 || a.N % bn) return set_error(LTXB_EINVAL, "gemm: N must be a multiple of 32");
+  if (a.b_int8 && bn == 32) return set_error(LTXB_EINVAL, "gemm: int8 weights need N % 128 == 0");
+  if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15) || (a.lda % 8) ||
+      (a.ldb % (a.b_int8 ? 16 : 8)) || (a.ldo % 8))
+    return set_error(LTXB_EINVAL, "gemm: operands must be 16-byte aligned with 16-byte row strides");
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda, GEMM_BK, GEMM_BM,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (a.b_int8)
+    rc = make_tmap_2d(&tb, a.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, a.ldb, GEMM_BK, bn,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+  else
+    rc = make_tmap_2d(&tb, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, a.ldb, GEMM_BK, bn,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (a.b_int8) {
+    if (bn == 256) return dispatch_epi<256, true>(ta, tb, a, st);
+    return dispatch_epi<128, true>(ta, tb, a, st);
+  }
+  if (bn == 256) return dispatch_epi<256, false>(ta, tb, a, st);
+  if (bn == 128) return dispatch_epi<128, false>(ta, tb, a, st);
+  return dispatch_epi<32, false>(ta, tb, a, st);
+}
+
+}  // namespace ltxb

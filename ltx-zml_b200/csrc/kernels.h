@@ -1,0 +1,120 @@
+// Internal interfaces between the C-ABI layer (ltxb.cu, block.cu) and the
+// kernels. Host-side only types; nothing here crosses the public boundary.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ltxb.h"
+
+namespace ltxb {
+
+// ---- errors (thread-local message, see ltxb_last_error) ----
+int set_error(int code, const char* fmt, ...);
+int set_cuda_error(cudaError_t e, const char* what);
+int sm_count();
+
+// ---- TMA descriptors ----
+// 2-D tensor map of a row-major [rows, cols] matrix with row stride `ld`
+// elements; box [box_rows, box_cols]. x = column (innermost), y = row.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int cols, int rows,
+                 int ld, int box_cols, int box_rows, CUtensorMapSwizzle swz);
+
+// ---- tcgen05 GEMM ----
+enum Epi : int {
+  EPI_BF16 = 0,          // out bf16 = acc (+ bias)
+  EPI_BF16_SSQ = 1,      // EPI_BF16 + per-(row, N tile) sum of squares for columns < ssq_cols
+  EPI_GELU_BF16 = 2,     // out bf16 = gelu_tanh(acc (+ bias))
+  EPI_RESID_F32 = 3,     // out f32 = xres + (acc + bias) * ada(ada_row)
+  EPI_GATE2SIG_F32 = 4,  // out f32 = 2 * sigmoid(acc + bias)
+  EPI_F32 = 5,           // out f32 = acc (+ bias)
+};
+
+struct GemmArgs {
+  const void* A;  // bf16 [M, K], row stride lda
+  int lda;
+  const void* B;  // bf16 or int8 [N, K], row stride ldb
+  int ldb;
+  int b_int8;
+  const void* scales;  // [N, K/128] f32 or bf16
+  int scale_bf16;
+  int M, N, K;
+  int bn;  // N tile (0 = auto)
+  int epi;
+  const void* bias;  // bf16 [N] or null
+  void* out;
+  int ldo;
+  // EPI_BF16_SSQ
+  float* ssq;
+  int ssq_cols;
+  int ssq_ld;
+  // EPI_RESID_F32
+  const float* xres;
+  int ldx;
+  const float* sst;    // [9, D]
+  const float* tstab;  // [K, 9, D]
+  const int* tidx;     // [M]
+  int ada_row;
+  int ada_d;
+};
+int gemm_tc(const GemmArgs& a, cudaStream_t st);
+
+// ---- flash attention (tcgen05) ----
+struct AttnArgs {
+  const void* q;  // bf16 [Tq, H, 128], row stride ldq elements
+  const void* k;  // bf16 [Tkv, H, 128], row stride ldk
+  const void* v;  // bf16 [Tkv, H, 128], row stride ldv
+  int ldq, ldk, ldv;
+  void* out;           // bf16 [Tq, H, 128] (contiguous)
+  const float* gate;   // f32 [Tq, ldg], column h = head h; or null
+  int ldg;
+  int Tq, Tkv, H;
+  float scale;
+  // ring-attention partial state (f32); when o_acc != null the kernel
+  // merges into (o_acc [Tq, H, 128], m [H, Tq], l [H, Tq]) instead of
+  // writing `out`, and `finalize` writes out = o_acc / l * gate.
+  float* o_acc;
+  float* m_state;
+  float* l_state;
+  int first;  // state starts empty
+};
+int attention_tc(const AttnArgs& a, cudaStream_t st);
+int attention_finalize(const AttnArgs& a, cudaStream_t st);
+
+// ---- elementwise / normalisation kernels ----
+// n = rms(x) * (1 + ada(r_scale)) + ada(r_shift) -> bf16 or f32 [T, D]
+int norm_modulate(const float* x, int T, int D, const float* sst, const float* tstab, const int* tidx, int r_shift,
+                  int r_scale, void* out, int out_f32, float* rms_copy, cudaStream_t st);
+// weightless rms only (s4_normed stage), f32 out
+int rms_rows(const float* x, int T, int D, float* out, cudaStream_t st);
+// q/k norm (+ optional RoPE) from raw bf16 projections and per-tile sums of squares
+int qk_norm_rope(const void* raw, int ld_raw, const float* ssq, int ssq_ld, int n_ssq, const void* w_bf16,
+                 const float* cos, const float* sin, int T, int D, void* out_bf16, float* out_f32, cudaStream_t st);
+// enc = ctx * (1 + (psst[1] + pts2[1])) + (psst[0] + pts2[0]) -> bf16 and/or f32
+int ctx_modulate(const float* ctx, int S, int D, const float* psst, const float* pts2, void* out_bf16,
+                 float* out_f32, cudaStream_t st);
+// int8 [N, K] + scales -> bf16 [N, K]
+int dequant_weights(const int8_t* q, const void* scales, int scale_bf16, int N, int K, void* out, cudaStream_t st);
+// f32 -> bf16 / bf16 -> f32 copies
+int cast_f32_bf16(const float* in, void* out, size_t n, cudaStream_t st);
+int cast_bf16_f32(const void* in, float* out, size_t n, cudaStream_t st);
+// q and k of self-attention normalised (+RoPE) in one pass sharing cos/sin
+int qk_norm_rope2(const void* raw_q, const void* raw_k, int ld_raw, const float* ssq_q, const float* ssq_k,
+                  int ssq_ld, int n_ssq, const void* wq, const void* wk, const float* cos, const float* sin, int T,
+                  int D, void* out_q, void* out_k, cudaStream_t st);
+
+// ---- f32 SIMT path (LTXB_MODE_F32) ----
+// C[M, N] = A[M, K] (f32) . W[N, K]^T (bf16 upcast) + bias, epilogues as Epi
+int gemm_f32(const float* A, int lda, const void* W, int M, int N, int K, const void* bias, int epi, float* out,
+             int ldo, float* ssq, int ssq_ld, const float* xres, const float* sst, const float* tstab,
+             const int* tidx, int ada_row, cudaStream_t st);
+// f32 attention: q/k/v f32 [T, H, 128] (row strides ld*) -> out f32 [Tq, H*128],
+// with optional gate [Tq, ldg]
+int attention_f32(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* out,
+                  const float* gate, int ldg, int Tq, int Tkv, int H, float scale, cudaStream_t st);
+// q/k norm (+RoPE) on f32 raw projections (ssq computed in-kernel)
+int qk_norm_rope_f32(const float* raw, int ld_raw, const void* w_bf16, const float* cos, const float* sin, int T,
+                     int D, float* out, cudaStream_t st);
+
+}  // namespace ltxb

@@ -1,0 +1,409 @@
+"""Python host mirror of the reference's block / loader interface over the
+C ABI of libltxb.so (include/ltxb.h).
+
+The reference drives its block through a compiled ZML executable
+(ltx/e2e_prod.zig:297-395) and uploads weights with ltx/loader.zig. This
+module gives the same operations, with the reference's names, on top of the
+sm_100a library:
+
+  Blob.open / check_layout / find_entry      ltx/loader.zig:45-129
+  build_block_bufs / build_quant_bufs        ltx/loader.zig:133-172
+  Block.s1NormMsa ... blockOut, wBlockOut     ltx/block.zig:248-353
+  QBlock.qBlockOutAll                        ltx/block.zig:544-574
+  attention (whileSdpa / sdpa)               ltx/block.zig:105-154, :234
+  dq_gemm (linQ)                             ltx/block.zig:462-477
+
+PyTorch provides device memory and streams only; every computation runs in
+libltxb.so. If the library is missing this module raises at import -- there
+is no fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import json
+import mmap
+import pathlib
+
+import numpy as np
+import torch
+
+_HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libltxb.so"
+
+OK = 0
+EINVAL, ECUDA, ENOMEM, ELAYOUT, EMISSING, EDTYPE, ENCCL, ETIMEOUT, EUNSUPPORTED = range(-1, -10, -1)
+DT_BF16, DT_F32, DT_I8 = 0, 1, 2
+MODE_F32, MODE_BF16, MODE_INT8 = 0, 1, 2
+QSET_REF, QSET_EXT = 0, 1
+STAGES = ["s1_norm_msa", "s1b_qnorm", "s2_attn1_nogate", "s3_attn1", "s4_after_sa", "s4_normed",
+          "s5_ca_out", "s6_ff_in", "s7_ff_out", "block_out"]
+_DT = {"BF16": DT_BF16, "F32": DT_F32, "I8": DT_I8}
+
+
+class LtxbError(RuntimeError):
+    """A failed library call: `.code` is the LTXB_E* status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ltxb error {code}: {msg}")
+        self.code = code
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is not built (run `make -C ltx-zml_b200` or __graft_entry__.build())")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    vp, i32, u64, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, ctypes.c_float
+    sig = {
+        "ltxb_init": (i32, [i32]),
+        "ltxb_last_error": (ctypes.c_char_p, []),
+        "ltxb_version": (ctypes.c_char_p, []),
+        "ltxb_device_status": (i32, [i32, ctypes.POINTER(ctypes.c_uint32)]),
+        "ltxb_blob_check_layout": (i32, [vp, i32, u64, ctypes.c_uint32]),
+        "ltxb_weights_upload": (i32, [i32, vp, u64, vp, i32, i32, i32, i32, i32, i32, ctypes.POINTER(vp)]),
+        "ltxb_weights_bytes": (u64, [vp]),
+        "ltxb_weights_free": (None, [vp]),
+        "ltxb_comm_id_bytes": (i32, []),
+        "ltxb_comm_get_id": (i32, [vp]),
+        "ltxb_comm_init": (i32, [vp, i32, i32, i32, ctypes.POINTER(vp)]),
+        "ltxb_comm_free": (None, [vp]),
+        "ltxb_block_workspace_bytes": (u64, [vp, vp]),
+        "ltxb_block_forward": (i32, [vp, vp, vp, vp]),
+        "ltxb_block_stage": (i32, [vp, vp, vp, i32, vp, vp]),
+        "ltxb_attention": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, f32, vp]),
+        "ltxb_dq_gemm": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, vp, u64, vp]),
+        "ltxb_gemm_bf16": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def _check(rc: int) -> None:
+    if rc != OK:
+        raise LtxbError(rc, lib.ltxb_last_error().decode(errors="replace"))
+
+
+def last_error() -> str:
+    return lib.ltxb_last_error().decode(errors="replace")
+
+
+def version() -> str:
+    return lib.ltxb_version().decode()
+
+
+def device_status(clear: bool = True) -> int:
+    """LTXB_OK or LTXB_ETIMEOUT (a bounded device wait expired). Syncs the device."""
+    site = ctypes.c_uint32(0)
+    return lib.ltxb_device_status(int(clear), ctypes.byref(site))
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    assert t.is_cuda and t.is_contiguous(), "tensors passed to libltxb must be contiguous CUDA tensors"
+    return t.data_ptr()
+
+
+def _stream(stream) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+# ---------------------------------------------------------------------------
+# blob + loader (ltx/loader.zig)
+# ---------------------------------------------------------------------------
+
+class _Entry(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int32), ("ndim", ctypes.c_int32),
+                ("shape", ctypes.c_int64 * 2), ("offset", ctypes.c_uint64), ("nbytes", ctypes.c_uint64)]
+
+
+def _entry_array(entries):
+    arr = (_Entry * len(entries))()
+    keep = []
+    for i, e in enumerate(entries):
+        nm = e["name"].encode()
+        keep.append(nm)
+        arr[i].name = nm
+        arr[i].dtype = _DT[e["dtype"]]
+        arr[i].ndim = len(e["shape"])
+        for j, d in enumerate(e["shape"][:2]):
+            arr[i].shape[j] = d
+        arr[i].offset = e["offset"]
+        arr[i].nbytes = e["nbytes"]
+    return arr, keep
+
+
+def normalize_name(name: str) -> str:
+    """ltx/loader.zig:102-119: '.' -> '_', '::' -> '_'."""
+    return name.replace("::", "_").replace(".", "_")
+
+
+class Blob:
+    """A packed block (blob.bin + blob_manifest.json, tools/pack_block.py),
+    memory-mapped like ltx/loader.zig:50-69."""
+
+    def __init__(self, data, manifest: dict):
+        self.data = data
+        self.manifest = manifest
+
+    @classmethod
+    def open(cls, directory, verify_digest: bool = False) -> "Blob":
+        d = pathlib.Path(directory)
+        man = json.loads((d / "blob_manifest.json").read_text())
+        path = d / "blob.bin"
+        if path.stat().st_size != man["total_bytes"]:
+            raise LtxbError(ELAYOUT, "BlobSizeMismatch")
+        with open(path, "rb") as f:
+            data = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) if man["total_bytes"] else b""
+        blob = cls(data, man)
+        if verify_digest and hashlib.sha256(data).hexdigest() != man["blob_sha256"]:
+            raise LtxbError(ELAYOUT, "BlobDigestMismatch")
+        return blob
+
+    @classmethod
+    def from_bytes(cls, data: bytes, entries: list[dict], align: int = 64, block: int = 0) -> "Blob":
+        return cls(data, {"align": align, "block": block, "total_bytes": len(data), "entries": entries})
+
+    def check_layout(self) -> None:
+        """ltx/loader.zig:73-82 through the library's check."""
+        arr, _keep = _entry_array(self.manifest["entries"])
+        _check(lib.ltxb_blob_check_layout(ctypes.addressof(arr), len(arr), self.manifest["total_bytes"],
+                                          self.manifest.get("align", 64)))
+
+    def find_entry(self, want: str) -> dict:
+        """ltx/loader.zig:122-129."""
+        for e in self.manifest["entries"]:
+            if normalize_name(e["name"]) == want:
+                return e
+        raise LtxbError(EMISSING, f"blob {self.manifest.get('block')}: no entry named {want}")
+
+
+class Weights:
+    """Device-resident weights of one block (an `ltxb_weights*`)."""
+
+    def __init__(self, handle, mode, hidden, ff, device):
+        self.handle = handle
+        self.mode = mode
+        self.D = hidden
+        self.FF = ff
+        self.H = hidden // 128
+        self.device = device
+
+    @property
+    def nbytes(self) -> int:
+        return lib.ltxb_weights_bytes(self.handle)
+
+    def free(self) -> None:
+        if self.handle:
+            lib.ltxb_weights_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def _upload(blob: Blob, block_idx: int, mode: int, qset: int, hidden: int, ff: int, device: int) -> Weights:
+    host = np.frombuffer(blob.data, dtype=np.uint8)
+    arr, _keep = _entry_array(blob.manifest["entries"])
+    h = ctypes.c_void_p()
+    _check(lib.ltxb_weights_upload(device, host.ctypes.data, host.size, ctypes.addressof(arr), len(arr),
+                                   block_idx, mode, qset, hidden, ff, ctypes.byref(h)))
+    return Weights(h, mode, hidden, ff, device)
+
+
+def build_block_bufs(blob: Blob, block_idx: int, mode: int = MODE_BF16, hidden: int = 4096, ff: int = 16384,
+                     device: int = 0) -> Weights:
+    """ltx/loader.zig:133-144: the 28 base tensors of a block, device-resident."""
+    return _upload(blob, block_idx, mode, QSET_REF, hidden, ff, device)
+
+
+def build_quant_bufs(blob: Blob, block_idx: int, qset: int = QSET_REF, hidden: int = 4096, ff: int = 16384,
+                     device: int = 0) -> Weights:
+    """ltx/loader.zig:158-172: int8 g128 pairs for the quantised linears."""
+    return _upload(blob, block_idx, MODE_INT8, qset, hidden, ff, device)
+
+
+# ---------------------------------------------------------------------------
+# communicator (sequence parallelism)
+# ---------------------------------------------------------------------------
+
+class Comm:
+    """NCCL communicator for the ring of K/V shards (one rank per GPU)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(lib.ltxb_comm_id_bytes())
+        _check(lib.ltxb_comm_get_id(buf))
+        return buf.raw
+
+    def __init__(self, uid: bytes, rank: int, nranks: int, device: int):
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(uid, len(uid))
+        _check(lib.ltxb_comm_init(buf, rank, nranks, device, ctypes.byref(h)))
+        self.handle, self.rank, self.nranks = h, rank, nranks
+
+    def free(self):
+        if self.handle:
+            lib.ltxb_comm_free(self.handle)
+            self.handle = None
+
+
+# ---------------------------------------------------------------------------
+# the block
+# ---------------------------------------------------------------------------
+
+class _Config(ctypes.Structure):
+    _fields_ = [("T", ctypes.c_int32), ("S", ctypes.c_int32), ("K", ctypes.c_int32), ("mode", ctypes.c_int32),
+                ("sp_rank", ctypes.c_int32), ("sp_size", ctypes.c_int32), ("comm", ctypes.c_void_p)]
+
+
+class _IO(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("out", ctypes.c_void_p), ("tstab", ctypes.c_void_p),
+                ("tidx", ctypes.c_void_p), ("ctx", ctypes.c_void_p), ("pts2", ctypes.c_void_p),
+                ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
+                ("workspace_bytes", ctypes.c_uint64)]
+
+
+class Block:
+    """A block bound to device weights: the reference's traced methods
+    (ltx/block.zig:248-353). Inputs are CUDA tensors:
+    x [T, D] f32, tstab [K, 9, D] f32, tidx [T] int32, ctx [S, D] f32,
+    pts2 [2, D] f32, cos/sin [T, H, 64] f32."""
+
+    def __init__(self, weights: Weights, comm: Comm | None = None):
+        self.w = weights
+        self.comm = comm
+        self._ws = None
+
+    def _cfg(self, T, S, K):
+        c = _Config(T, S, K, self.w.mode, self.comm.rank if self.comm else 0,
+                    self.comm.nranks if self.comm else 1, self.comm.handle if self.comm else None)
+        return c
+
+    def workspace_bytes(self, T: int, S: int, K: int = 1) -> int:
+        c = self._cfg(T, S, K)
+        return lib.ltxb_block_workspace_bytes(self.w.handle, ctypes.byref(c))
+
+    def _workspace(self, nbytes: int, device) -> torch.Tensor:
+        if self._ws is None or self._ws.numel() < nbytes or self._ws.device != device:
+            self._ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+        return self._ws
+
+    def _io(self, x, tstab, tidx, ctx, pts2, cos, sin, out):
+        T, S, K = x.shape[0], ctx.shape[0], tstab.shape[0]
+        c = self._cfg(T, S, K)
+        nbytes = lib.ltxb_block_workspace_bytes(self.w.handle, ctypes.byref(c))
+        ws = self._workspace(nbytes, x.device)
+        base = ws.data_ptr()
+        aligned = (base + 255) & ~255
+        io = _IO(_ptr(x), _ptr(out), _ptr(tstab), _ptr(tidx), _ptr(ctx), _ptr(pts2), _ptr(cos), _ptr(sin),
+                 aligned, ws.numel() - (aligned - base))
+        return c, io
+
+    def forward(self, x, tstab, tidx, ctx, pts2, cos, sin, out=None, stream=None) -> torch.Tensor:
+        """ltxb_block_forward: the whole block with blockwise attention."""
+        out = torch.empty_like(x) if out is None else out
+        c, io = self._io(x, tstab, tidx, ctx, pts2, cos, sin, out)
+        _check(lib.ltxb_block_forward(self.w.handle, ctypes.byref(io), ctypes.byref(c), _stream(stream)))
+        return out
+
+    def stage(self, stage: int | str, x, tstab, tidx, ctx, pts2, cos, sin, stream=None) -> torch.Tensor:
+        si = STAGES.index(stage) if isinstance(stage, str) else stage
+        out = torch.empty_like(x)
+        scratch = torch.empty_like(x)
+        c, io = self._io(x, tstab, tidx, ctx, pts2, cos, sin, scratch)
+        _check(lib.ltxb_block_stage(self.w.handle, ctypes.byref(io), ctypes.byref(c), si, _ptr(out),
+                                    _stream(stream)))
+        return out
+
+    # the reference's method names (ltx/block.zig:248-353)
+    def blockOut(self, x, tstab, tidx, ctx, pts2, cos, sin):
+        return self.forward(x, tstab, tidx, ctx, pts2, cos, sin)
+
+    def wBlockOut(self, x, tstab, tidx, ctx, pts2, cos, sin):
+        """Same function as blockOut: attention here is always the blockwise
+        online softmax, which the reference gates against dense at 1e-5."""
+        return self.forward(x, tstab, tidx, ctx, pts2, cos, sin)
+
+    def s1NormMsa(self, *a):
+        return self.stage("s1_norm_msa", *a)
+
+    def s1bQnorm(self, *a):
+        return self.stage("s1b_qnorm", *a)
+
+    def s2Attn1NoGate(self, *a):
+        return self.stage("s2_attn1_nogate", *a)
+
+    def s3Attn1(self, *a):
+        return self.stage("s3_attn1", *a)
+
+    def s4AfterSa(self, *a):
+        return self.stage("s4_after_sa", *a)
+
+    def s4Normed(self, *a):
+        return self.stage("s4_normed", *a)
+
+    def s5CaOut(self, *a):
+        return self.stage("s5_ca_out", *a)
+
+    def s6FfIn(self, *a):
+        return self.stage("s6_ff_in", *a)
+
+    def s7FfOut(self, *a):
+        return self.stage("s7_ff_out", *a)
+
+
+class QBlock(Block):
+    """ltx/block.zig:481-574: the block with int8 g128 linears."""
+
+    def qBlockOutAll(self, x, tstab, tidx, ctx, pts2, cos, sin):
+        assert self.w.mode == MODE_INT8
+        return self.forward(x, tstab, tidx, ctx, pts2, cos, sin)
+
+
+# ---------------------------------------------------------------------------
+# standalone operators
+# ---------------------------------------------------------------------------
+
+def attention(q, k, v, gate=None, scale: float | None = None, out=None, stream=None) -> torch.Tensor:
+    """softmax(q k^T * scale) v per head; q [Tq, H, 128], k/v [Tkv, H, 128] bf16."""
+    Tq, H, hd = q.shape
+    assert hd == 128 and q.dtype == torch.bfloat16
+    scale = 1.0 / np.sqrt(hd) if scale is None else scale
+    out = torch.empty_like(q) if out is None else out
+    _check(lib.ltxb_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(gate), Tq, k.shape[0], H, float(scale),
+                              _stream(stream)))
+    return out
+
+
+def dq_gemm(a, wq, scales, bias=None, fused: bool = True, out=None, workspace=None, stream=None) -> torch.Tensor:
+    """linQ: a [M, K] bf16 . dequant(wq [N, K] int8, scales [N, K/128])^T (+ bias) -> bf16 [M, N]."""
+    M, K = a.shape
+    N = wq.shape[0]
+    sdt = DT_BF16 if scales.dtype == torch.bfloat16 else DT_F32
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device) if out is None else out
+    if not fused and workspace is None:
+        workspace = torch.empty(N * K * 2, dtype=torch.uint8, device=a.device)
+    _check(lib.ltxb_dq_gemm(_ptr(a), _ptr(wq), _ptr(scales), sdt, _ptr(bias), _ptr(out), M, N, K, int(fused),
+                            _ptr(workspace), 0 if workspace is None else workspace.numel(), _stream(stream)))
+    return out
+
+
+def gemm_bf16(a, w, bias=None, out=None, stream=None) -> torch.Tensor:
+    """lin on tcgen05: a [M, K] bf16 . w [N, K]^T (+ bias) -> bf16 [M, N]."""
+    M, K = a.shape
+    N = w.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device) if out is None else out
+    _check(lib.ltxb_gemm_bf16(_ptr(a), _ptr(w), _ptr(bias), _ptr(out), M, N, K, _stream(stream)))
+    return out

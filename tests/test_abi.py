@@ -1,0 +1,107 @@
+"""CPU tests of the C-ABI boundary: libltxb.so loads, exports exactly what
+include/ltxb.h declares, and its host-only entry points (no GPU needed)
+behave like the reference's loader checks (ltx/loader.zig:73-82)."""
+
+import ctypes
+import json
+import pathlib
+import re
+import subprocess
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "ltxb.h"
+GOLD = ROOT / "tests" / "golden" / "ref_tools"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ltxb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    fns = declared_functions()
+    for must in ("ltxb_init", "ltxb_weights_upload", "ltxb_weights_free", "ltxb_block_forward",
+                 "ltxb_attention", "ltxb_dq_gemm", "ltxb_last_error", "ltxb_comm_init"):
+        assert must in fns
+
+
+def test_library_exports_every_declared_symbol():
+    import ltxb
+    out = subprocess.run(["nm", "-D", "--defined-only", str(ltxb.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\sT\s(ltxb_[a-z0-9_]+)$", out, flags=re.M))
+    missing = [f for f in declared_functions() if f not in exported]
+    assert not missing, f"declared in ltxb.h but not exported: {missing}"
+    for f in declared_functions():
+        assert hasattr(ltxb.lib, f)
+
+
+def test_version_and_error_string():
+    import ltxb
+    assert "sm_100a" in ltxb.version()
+    assert isinstance(ltxb.last_error(), str)
+
+
+def _golden_blob():
+    import ltxb
+    return ltxb.Blob.open(GOLD, verify_digest=True)
+
+
+def test_blob_open_and_layout_ok():
+    b = _golden_blob()
+    b.check_layout()
+    e = b.find_entry("transformer_blocks_0_attn1_to_q_weight_q8scale")
+    assert e["dtype"] == "F32" and e["shape"] == [32, 2]
+
+
+@pytest.mark.parametrize("mutate,err", [
+    (lambda es: es[1].__setitem__("offset", es[1]["offset"] + 4), "Misaligned"),
+    (lambda es: es[1].__setitem__("offset", es[1]["offset"] + 64), "LayoutGap"),
+    (lambda es: es.pop(), "TrailingBytes"),
+])
+def test_blob_layout_errors(mutate, err):
+    import ltxb
+    man = json.loads((GOLD / "blob_manifest.json").read_text())
+    entries = [dict(e) for e in man["entries"]]
+    mutate(entries)
+    b = ltxb.Blob(b"", {"align": 64, "total_bytes": man["total_bytes"], "entries": entries})
+    with pytest.raises(ltxb.LtxbError) as ei:
+        b.check_layout()
+    assert ei.value.code == ltxb.ELAYOUT and err in str(ei.value)
+
+
+def test_missing_entry_error():
+    import ltxb
+    with pytest.raises(ltxb.LtxbError) as ei:
+        _golden_blob().find_entry("transformer_blocks_0_nope")
+    assert ei.value.code == ltxb.EMISSING
+
+
+def test_blob_size_mismatch(tmp_path):
+    import ltxb
+    (tmp_path / "blob.bin").write_bytes((GOLD / "blob.bin").read_bytes()[:-1])
+    (tmp_path / "blob_manifest.json").write_text((GOLD / "blob_manifest.json").read_text())
+    with pytest.raises(ltxb.LtxbError, match="BlobSizeMismatch"):
+        ltxb.Blob.open(tmp_path)
+
+
+def test_blob_digest_mismatch(tmp_path):
+    import ltxb
+    data = bytearray((GOLD / "blob.bin").read_bytes())
+    data[100] ^= 1
+    (tmp_path / "blob.bin").write_bytes(bytes(data))
+    (tmp_path / "blob_manifest.json").write_text((GOLD / "blob_manifest.json").read_text())
+    with pytest.raises(ltxb.LtxbError, match="BlobDigestMismatch"):
+        ltxb.Blob.open(tmp_path, verify_digest=True)
+
+
+def test_null_arguments_rejected():
+    import ltxb
+    assert ltxb.lib.ltxb_blob_check_layout(None, 3, 0, 64) == ltxb.EINVAL
+    h = ctypes.c_void_p()
+    assert ltxb.lib.ltxb_weights_upload(0, None, 0, None, 0, 0, 0, 0, 4096, 16384, ctypes.byref(h)) == ltxb.EINVAL
+    ltxb.lib.ltxb_weights_free(None)
+    ltxb.lib.ltxb_comm_free(None)

@@ -1,0 +1,149 @@
+"""GPU parity tests of the whole block through the C ABI, stage by stage, in
+the reference's three precisions (ltx/block_conformance.zig's fence):
+
+* f32 mode (reference `Block`): every stage within rel-RMS 1e-5 of the f64
+  oracle -- BASELINE config 0 at full width (D 4096, T 1024, S 128).
+* bf16 mode and int8 mode (reference `QBlock`, same dequantised weights in the
+  oracle): rel-RMS <= 5e-3 and no worse than a torch-bf16 run of the same
+  block (the reference's own "bf16 deployment floor",
+  tools/make_oracle_bundle.py:184-200).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import helpers
+from oracle import ltx_block_ref as ref
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-5
+LOW_TOL = 5e-3
+
+
+def _run_stages(w, inp_t, stages):
+    import ltxb
+    blk = ltxb.Block(w)
+    out = {}
+    for s in stages:
+        out[s] = blk.stage(s, *inp_t).double().cpu().numpy()
+    torch.cuda.synchronize()
+    assert ltxb.device_status() == ltxb.OK
+    return out
+
+
+def _check(got, want, tol, label):
+    worst = {}
+    for s, g in got.items():
+        assert np.isfinite(g).all(), f"{label}/{s}: non-finite values"
+        worst[s] = ref.rel_rms(g, want[s])
+    bad = {s: e for s, e in worst.items() if e > tol}
+    assert not bad, f"{label}: rel-RMS over {tol}: {bad} (all: {worst})"
+    return worst
+
+
+SMALL = dict(d=256, ff=512, grid=(2, 4, 16), s=16)
+
+
+@pytest.mark.parametrize("adaln,k_rows,rope", [("random", 3, "axes"), ("mlp", 1, "ltx")])
+def test_f32_small_all_stages(cuda, adaln, k_rows, rope):
+    import ltxb
+    geom, bw, data, ent, _ = helpers.weights_case(SMALL["d"], SMALL["ff"], 0, None)
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 0, rope, k_rows, adaln)
+    want = helpers.oracle_stages(bw, inp)
+    w = helpers.upload(data, ent, geom, ltxb.MODE_F32)
+    got = _run_stages(w, helpers.to_cuda(inp, cuda), ref.STAGES)
+    _check(got, want, F32_TOL, "f32-small")
+
+
+def test_f32_config0(cuda):
+    """D 4096, 32x128 heads, T 1024 on 8x8x16, S 128, FFN
+    16384, RoPE 44/42/42, timestep 0.5 through the adaln MLP."""
+    import ltxb
+    geom, bw, data, ent, _ = helpers.weights_case(4096, 16384, 0, None)
+    inp = helpers.inputs_case(4096, (8, 8, 16), 128, 0)
+    want = helpers.oracle_stages(bw, inp)
+    w = helpers.upload(data, ent, geom, ltxb.MODE_F32)
+    got = _run_stages(w, helpers.to_cuda(inp, cuda), ref.STAGES)
+    _check(got, want, F32_TOL, "f32-config0")
+    w.free()
+
+
+def _bf16_floor(bw, inp, qset=None):
+    """The block run in torch bfloat16 on CPU (weights, inputs and every op in
+    bf16), compared with f64: the reference's bf16 path analogue."""
+    want = helpers.oracle_stages(bw, inp, qset)["block_out"]
+    b16 = helpers.oracle_stages(bw, inp, qset, dtype=torch.bfloat16)["block_out"]
+    return ref.rel_rms(b16, want)
+
+
+@pytest.mark.parametrize("mode", ["bf16", "int8", "int8-ext-bf16scale"])
+def test_lowp_small_all_stages(cuda, mode):
+    import ltxb
+    quant = None if mode == "bf16" else "int8"
+    sdt = "bf16" if "bf16scale" in mode else "f32"
+    qext = "ext" in mode
+    geom, bw, data, ent, qset = helpers.weights_case(SMALL["d"], SMALL["ff"], 1, quant, sdt, qext)
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 1, "axes", 3, "random")
+    oq = qset if quant else None
+    want = helpers.oracle_stages(bw, inp, oq)
+    w = helpers.upload(data, ent, geom, ltxb.MODE_BF16 if quant is None else ltxb.MODE_INT8, qext)
+    got = _run_stages(w, helpers.to_cuda(inp, cuda), ref.STAGES)
+    worst = _check(got, want, LOW_TOL, mode)
+    floor = _bf16_floor(bw, inp, oq)
+    assert worst["block_out"] <= max(floor, 1e-4), f"{mode}: {worst['block_out']} worse than torch-bf16 {floor}"
+
+
+@pytest.mark.parametrize("mode", ["bf16", "int8"])
+def test_lowp_config0(cuda, mode):
+    """Config-0 architecture at T = 1024 in bf16 / int8 (config 3's recipe:
+    outliers, g128, f32 scales), block output and the conformance stages."""
+    import ltxb
+    quant = None if mode == "bf16" else "int8"
+    geom, bw, data, ent, qset = helpers.weights_case(4096, 16384, 0, quant)
+    inp = helpers.inputs_case(4096, (8, 8, 16), 128, 0)
+    oq = qset if quant else None
+    want = helpers.oracle_stages(bw, inp, oq)
+    w = helpers.upload(data, ent, geom, ltxb.MODE_BF16 if quant is None else ltxb.MODE_INT8)
+    got = _run_stages(w, helpers.to_cuda(inp, cuda), ref.STAGES)
+    worst = _check(got, want, LOW_TOL, f"{mode}-config0")
+    floor = _bf16_floor(bw, inp, oq)
+    assert worst["block_out"] <= floor, f"{mode}: {worst['block_out']} worse than torch-bf16 {floor}"
+    w.free()
+
+
+def test_block_forward_deterministic_and_aliasing(cuda):
+    import ltxb
+    geom, bw, data, ent, _ = helpers.weights_case(SMALL["d"], SMALL["ff"], 2, "int8")
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 2, "axes", 3, "random")
+    w = helpers.upload(data, ent, geom, ltxb.MODE_INT8)
+    blk = ltxb.QBlock(w)
+    t = helpers.to_cuda(inp, cuda)
+    a = blk.qBlockOutAll(*t)
+    b = blk.qBlockOutAll(*t)
+    x2 = t[0].clone()
+    blk.forward(x2, *t[1:], out=x2)  # out aliases x
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert torch.equal(a, x2)
+
+
+def test_upload_errors(cuda):
+    import ltxb
+    geom, bw, data, ent, _ = helpers.weights_case(SMALL["d"], SMALL["ff"], 0, None)
+    # int8 mode on a blob without ::q8 companions -> MissingEntry
+    with pytest.raises(ltxb.LtxbError) as ei:
+        helpers.upload(data, ent, geom, ltxb.MODE_INT8)
+    assert ei.value.code == ltxb.EMISSING
+    # wrong geometry -> dtype/shape error
+    with pytest.raises(ltxb.LtxbError) as ei:
+        ltxb.build_block_bufs(ltxb.Blob.from_bytes(data, ent), 0, hidden=512, ff=512)
+    assert ei.value.code == ltxb.EDTYPE
+    # mode mismatch between weights and config
+    w = helpers.upload(data, ent, geom, ltxb.MODE_BF16)
+    blk = ltxb.Block(w)
+    blk.w.mode = ltxb.MODE_F32
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 0, "axes", 3, "random")
+    with pytest.raises(ltxb.LtxbError):
+        blk.forward(*helpers.to_cuda(inp, cuda))
