@@ -1,0 +1,436 @@
+#!/usr/bin/env python3
+"""Benchmark: one int8-weight LTX-2.5 DiT block at T = 28,160 video tokens
+(22x32x40 latent grid, D 4096, 32x128 heads, FFN 16384,
+128 text tokens, int8 grouped-128 weights with bf16 scales for the q/k/v,
+output and FFN projections), on 1..N B200s of one node with the tokens
+sharded across ranks (sequence-parallel ring attention over NVLink).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched by torchrun (one rank per GPU). Rank 0 prints one JSON
+line. A step is one block forward over all 28,160 tokens; `value` is the
+whole-job throughput in TFLOP/s of algorithmic work (26.30 TFLOP per block).
+
+`--impl reference` times the CPU restatement of the reference block
+(oracle/, torch f32 on all host cores) on a bounded sample of the workload:
+the reference itself is Zig on ZML/XLA and cannot be built on this machine.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "ltx-zml_b200")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+T_TOTAL, GRID, S, D, FF, H = 28160, (22, 32, 40), 128, 4096, 16384, 32
+METRIC = "dit_block_tflops_28k_int8w"
+CPU_SAMPLE_T = 1024  # config-0 token count for the CPU sample
+
+
+def block_flops(T: int, s: int = S, d: int = D, ff: int = FF, h: int = H) -> float:
+    """Algorithmic FLOPs of one block over T tokens (multiply-add = 2):
+    self q/k/v/o 8TD^2, cross q/o 4TD^2, cross k/v 4SD^2, the two gate
+    linears 4TDH, FFN 4TD.FF, self-attention 4T^2 D, cross-attention 4TSD."""
+    return (8 * T * d * d + 4 * T * d * d + 4 * s * d * d + 4 * T * d * h + 4 * T * d * ff
+            + 4 * T * T * d + 4 * T * s * d)
+
+
+def phase_work(T_loc: int, T_all: int) -> dict:
+    """(kind, amount per call) per library phase: FLOPs for tensor-core
+    phases, bytes for the bandwidth-bound ones (minimum HBM traffic)."""
+    return {
+        "gemm_qkv1": ("tensor", 2 * T_loc * D * 3 * D),
+        "gemm_gate1": ("tensor", 2 * T_loc * D * 32),
+        "attn_self": ("tensor", 4 * T_loc * T_all * D),
+        "gemm_o1": ("tensor", 2 * T_loc * D * D),
+        "gemm_q2": ("tensor", 2 * T_loc * D * D),
+        "gemm_gate2": ("tensor", 2 * T_loc * D * 32),
+        "attn_cross": ("tensor", 4 * T_loc * S * D),
+        "gemm_o2": ("tensor", 2 * T_loc * D * D),
+        "gemm_ff1": ("tensor", 2 * T_loc * D * FF),
+        "gemm_ff2": ("tensor", 2 * T_loc * FF * D),
+        "prompt_kv": ("tensor", 2 * S * D * 2 * D),
+        # x f32 read + n bf16 write
+        "norm_msa": ("hbm", T_loc * D * (4 + 2)),
+        "norm_ca": ("hbm", T_loc * D * (4 + 2)),
+        "norm_mlp": ("hbm", T_loc * D * (4 + 2)),
+        # q,k bf16 read + write, cos/sin f32 [T, H, 64] read
+        "qk_norm_rope": ("hbm", T_loc * D * 2 * 4 + 2 * T_loc * H * 64 * 4),
+        "qk_norm2": ("hbm", T_loc * D * 2 * 2),
+    }
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return {"hbm": j["hbm_gbs"], "bf16": j["bf16_tflops"], "bf16_sustained": j["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(p[1]), max=float(p[2]), power=float(p[3]), hw=p[5], hwt=p[6],
+                                 swt=p[7], swp=p[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        load = [r for r in rows if r["power"] > 300] or rows
+        reasons = set()
+        for r in load:
+            for k, nm in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                          ("swp", "sw_power_cap")):
+                if r[k].lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["max"] for r in rows),
+                "samples": len(load), "power_w_max": max(r["power"] for r in rows), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic config-3 block, generated on the GPU
+# ---------------------------------------------------------------------------
+
+QUANT_FIELDS = ("q1_w", "k1_w", "v1_w", "o1_w", "q2_w", "k2_w", "v2_w", "o2_w", "ff1_w", "ff2_w")
+
+
+def make_blob(device, seed: int = 0):
+    """Config-3 weights: N(0, 0.02) (norm weights 1 + N(0, 0.02), tables f32),
+    int8 g128 for QUANT_FIELDS after scaling 0.5% of input channels x20,
+    symmetric absmax/127 scales rounded to bf16; packed in the reference blob
+    format (name-sorted, 64-byte aligned)."""
+    from oracle import blob as oblob
+    from oracle import ltx_block_ref as ref
+    geom = ref.Geometry(d=D, ff=FF)
+    g = torch.Generator(device=device)
+    tensors = []
+    for i, (field, _stem, dims) in enumerate(ref.WEIGHT_SPECS):
+        shape = geom.dims(dims)
+        g.manual_seed(seed * 1000 + i)
+        w = torch.randn(*shape, generator=g, device=device) * 0.02
+        name = f"transformer_blocks.0.{oblob.DOTTED[field]}"
+        if field in ref.F32_FIELDS:
+            tensors.append((name, "F32", list(shape), w.cpu().numpy().tobytes()))
+            continue
+        if field.startswith(("qn", "kn")):
+            w = w + 1.0
+        if field in QUANT_FIELDS:
+            k = shape[1]
+            cols = torch.randperm(k, generator=g, device=device)[: max(1, round(0.005 * k))]
+            w[:, cols] *= 20.0
+            wg = w.view(shape[0], k // 128, 128)
+            amax = wg.abs().amax(-1, keepdim=True)
+            sc = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax)).to(torch.bfloat16)
+            q = torch.clamp(torch.round(wg / sc.float()), -128, 127).to(torch.int8).view(shape)
+            tensors.append((name + "::q8", "I8", list(shape), q.cpu().numpy().tobytes()))
+            tensors.append((name + "::q8scale", "BF16", [shape[0], k // 128],
+                            sc.view(torch.int16).view(shape[0], k // 128).cpu().numpy().tobytes()))
+        else:
+            tensors.append((name, "BF16", list(shape), w.to(torch.bfloat16).view(torch.int16).cpu().numpy().tobytes()))
+    data, entries = oblob.pack(tensors)
+    ent = [dict(name=e.name, dtype=e.dtype, shape=e.shape, offset=e.offset, nbytes=e.nbytes) for e in entries]
+    return data, ent
+
+
+def make_inputs(device, rank: int, world: int, seed: int = 0):
+    """This rank's token slice of x [T, D], the 44/42/42 RoPE tables on the
+    22x32x40 grid, tstab [1, 9, D] / tidx, ctx [128, D], pts2 [2, D]."""
+    T = T_TOTAL // world
+    r0 = rank * T
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 17)
+    x_all = torch.randn(T_TOTAL, D, generator=g, device=device)
+    x = x_all[r0:r0 + T].contiguous()
+    del x_all
+    g.manual_seed(seed + 18)
+    ctx = torch.randn(S, D, generator=g, device=device)
+    tstab = torch.randn(1, 9, D, generator=g, device=device) * 0.1
+    pts2 = torch.randn(2, D, generator=g, device=device) * 0.1
+    tidx = torch.zeros(T, dtype=torch.int32, device=device)
+    f, hh, ww = GRID
+    t = torch.arange(r0, r0 + T, device=device)
+    pos = torch.stack([t // (hh * ww), (t // ww) % hh, t % ww], dim=1).double()
+    ang = []
+    for axis, dims in enumerate((44, 42, 42)):
+        inv = 10000.0 ** (-2.0 * torch.arange(dims // 2, device=device, dtype=torch.float64) / dims)
+        ang.append(pos[:, axis:axis + 1] * inv[None])
+    a = torch.cat(ang, dim=1)
+    cos = torch.cos(a).float()[:, None, :].expand(T, H, 64).contiguous()
+    sin = torch.sin(a).float()[:, None, :].expand(T, H, 64).contiguous()
+    return x, tstab, tidx, ctx, pts2, cos, sin
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle's block in torch f32 on the host cores
+# ---------------------------------------------------------------------------
+
+def cpu_block_sample(steps: int, warmup: int):
+    """Times the CPU restatement (oracle.ltx_block_ref.QBlock, torch f32, all
+    host threads) on the config-0 token count, same architecture and int8
+    weights. Returns (TFLOP/s, ms per sample block, threads)."""
+    from oracle import inputs as oin
+    from oracle import ltx_block_ref as ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    geom = ref.Geometry(d=D, ff=FF)
+    bw = oin.make_weights(geom, 0, quant="int8", scale_dtype="bf16", qset=ref.Q8_FIELDS_EXT)
+    inp = oin.make_inputs(geom, grid=(8, 8, 16), s=S, seed=0, adaln="random")
+    blk = ref.QBlock(bw, torch.float32, qset=ref.Q8_FIELDS_EXT)
+    args = inp.torch(torch.float32)
+    with torch.no_grad():
+        for _ in range(warmup):
+            blk.w_block_out(*args)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            blk.w_block_out(*args)
+        dt = (time.perf_counter() - t0) / max(1, steps)
+    return block_flops(CPU_SAMPLE_T) / dt / 1e12, dt * 1e3, torch.get_num_threads()
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    # bounded sample: at most 3 timed CPU blocks (each ~1-3 s)
+    tflops, ms, cores = cpu_block_sample(min(steps, 3), min(warm, 1))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tflops, 4), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(block_flops(T_TOTAL) / (tflops * 1e12) * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "int8 DiT block, T=28160 (22x32x40), D=4096, S=128, FF=16384",
+                   "sample": f"CPU restatement at T={CPU_SAMPLE_T}; ms_per_step extrapolated at the sample's TFLOP/s"},
+        "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": f"oracle QBlock (torch f32, {cores} threads), T={CPU_SAMPLE_T}, "
+                                   f"{ms:.0f} ms per block"},
+        "e2e": {"value": round(tflops, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference (Zig on ZML/XLA) cannot be built here; its CPU path is timed through the "
+                "oracle restatement",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import ltxb
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    comm = None
+    if world > 1:
+        uid = [ltxb.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = ltxb.Comm(uid[0], rank, world, local_rank)
+    data, ent = make_blob(dev)
+    w = ltxb.build_quant_bufs(ltxb.Blob.from_bytes(data, ent), 0, qset=ltxb.QSET_EXT, hidden=D, ff=FF,
+                              device=local_rank)
+    del data
+    blk = ltxb.QBlock(w, comm)
+    x, tstab, tidx, ctx, pts2, cos, sin = make_inputs(dev, rank, world)
+    T = x.shape[0]
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        blk.forward(x, tstab, tidx, ctx, pts2, cos, sin, out=out)
+    barrier()
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ltxb.profile_collect(reset=True)
+    ltxb.profile_enable(True)
+    l0 = ltxb.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        blk.forward(x, tstab, tidx, ctx, pts2, cos, sin, out=out)
+    e1.record(stream)
+    barrier()
+    launches = ltxb.launch_count() - l0
+    ltxb.profile_enable(False)
+    phases = ltxb.profile_collect(reset=True)
+    ms = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop() if sampler else None
+    status = ltxb.device_status(clear=True)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # end to end through the public API with host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_in = torch.empty_like(x)
+    e2e_steps = max(1, min(args.steps, 5))
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(e2e_steps):
+        x_in.copy_(x_host, non_blocking=True)
+        blk.forward(x_in, tstab, tidx, ctx, pts2, cos, sin, out=out)
+        out_host.copy_(out, non_blocking=True)
+    e3.record(stream)
+    barrier()
+    e2e_ms = e2.elapsed_time(e3) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    if rank == 0:
+        pk = peaks()
+        flops = block_flops(T_TOTAL)
+        value = flops / (ms * 1e-3) / 1e12
+        work = phase_work(T, T_TOTAL)
+        steps = args.steps
+        table = {}
+        for nm, (tot_ms, nl, calls) in phases.items():
+            per = tot_ms / max(1, calls)
+            kind, amount = work.get(nm, ("other", 0))
+            row = {"ms": round(per, 4), "share": round(tot_ms / (ms * steps), 4), "launches_per_call": nl // max(1, calls)}
+            if kind == "tensor" and amount:
+                row["tflops"] = round(amount / (per * 1e-3) / 1e12, 1)
+            elif kind == "hbm" and amount:
+                row["gbs"] = round(amount / (per * 1e-3) / 1e9, 1)
+            table[nm] = row
+        top = max(table, key=lambda k: table[k]["ms"]) if table else None
+        roofline = None
+        if top:
+            kind, amount = work.get(top, ("tensor", 0))
+            per_s = table[top]["ms"] * 1e-3
+            if kind == "hbm":
+                ach = amount / per_s / 1e9
+                roofline = {"kernel": top, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm"],
+                            "unit": "GB/s", "frac": round(ach / pk["hbm"], 4)}
+            else:
+                ach = amount / per_s / 1e12
+                roofline = {"kernel": top, "bound": "tensor", "achieved": round(ach, 1), "peak": pk["bf16_sustained"],
+                            "unit": "TFLOP/s", "frac": round(ach / pk["bf16_sustained"], 4),
+                            "frac_of_burst_peak": round(ach / pk["bf16"], 4),
+                            "algorithmic_per_launch": amount}
+            tr = ROOT / "profiles" / "ncu_traffic.json"
+            roofline["traffic"] = None
+            if tr.exists():
+                tj = json.loads(tr.read_text())
+                if top in tj:
+                    roofline["traffic"] = tj[top]["bytes_per_launch"]
+            roofline["peak_source"] = pk["source"] + " (MEASURED_PEAKS.json; sustained for a kernel inside a long step)"
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "int8 DiT block, T=28160 (22x32x40), D=4096, 32x128 heads, S=128, FF=16384",
+                       "weights": "int8 g128 (bf16 scales) q/k/v/o x2 + FFN; bf16 gates/norms/biases",
+                       "parallelism": f"sp{world} (ring attention over NVLink)" if world > 1 else "single GPU",
+                       "tokens_per_rank": T, "l2": "inputs larger than L2 (x 461 MB f32, weights 0.7 GB)"},
+            "frac_of_peak": round(value / world / pk["bf16"], 4),
+            "frac_of_sustained_peak": round(value / world / pk["bf16_sustained"], 4),
+            "roofline": roofline,
+            "phases": table,
+            "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": T_TOTAL * D * 4,
+                    "d2h_bytes_per_step": T_TOTAL * D * 4},
+            "gpu_launches": launches,
+            "gpu_launches_per_step": launches // max(1, args.steps),
+            "clocks": clocks,
+            "device_status": status,
+        }
+        if world == 1 and not args.no_cpu:
+            try:
+                tf, cms, cores = cpu_block_sample(1, 1)
+                line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                        "sample": f"oracle QBlock, torch f32 on {cores} host threads, T={CPU_SAMPLE_T}"
+                                                  f" (config-0 shape), {cms:.0f} ms per block"}
+            except Exception as exc:  # the baseline is reported, never required
+                line["cpu_baseline"] = {"value": None, "error": repr(exc)[:200]}
+        print(json.dumps(line), flush=True)
+    w.free()
+    if comm is not None:
+        comm.free()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}; using WORLD_SIZE", file=sys.stderr)
+    if T_TOTAL % world or (T_TOTAL // world) % 64:
+        raise SystemExit(f"T={T_TOTAL} does not shard over {world} ranks")
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

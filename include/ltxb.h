@@ -91,6 +91,24 @@ const char* ltxb_version(void);
  * Synchronises the device. */
 int ltxb_device_status(int clear, uint32_t* site);
 
+/* ---- measurement -------------------------------------------------------- */
+
+/* Kernels this library has launched in this process (all devices). */
+uint64_t ltxb_launch_count(void);
+
+/* Per-phase device timing of the block's launch sequence (CUDA events around
+ * each phase on the caller's stream). Off by default; the reference's
+ * equivalent is host wall-clock around synchronised calls
+ * (ltx/smoke.zig:243-254). */
+int ltxb_profile_enable(int on);
+
+/* Synchronise the recorded events and accumulate them per phase name.
+ * Writes up to max_phases rows: names (name_stride bytes each), total device
+ * milliseconds, kernel launches, and calls; returns the number of phases
+ * (or a negative error). reset != 0 clears the accumulators afterwards. */
+int ltxb_profile_collect(int max_phases, char* names, int name_stride, double* total_ms, uint64_t* launches,
+                         int* calls, int reset);
+
 /* ---- weights (ltx/loader.zig:133-172) ---------------------------------- */
 
 /* One entry of a packed block blob, in the format of tools/pack_block.py:

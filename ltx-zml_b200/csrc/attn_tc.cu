@@ -2,21 +2,28 @@
 // of the reference's whileSdpa (ltx/block.zig:105-154) and the dense
 // zml.nn.sdpa it agrees with (ltx/block.zig:234, gate ltx/block_conformance.zig:406).
 //
-// CTA = one 128-row query tile of one head, 256 threads:
-//   warp 0      TMA producer: Q once, then K_j / V_j tiles (128 x 128) into a
-//               2-stage ring (separate K and V barriers)
-//   warp 1      TMEM owner + single-thread MMA issuer:
-//                 S_j = Q K_j^T  -> TMEM (two S buffers, 128 columns each)
-//                 O  += P_j V_j  -> TMEM (128 columns), P_j from shared memory
-//   warps 4..7  softmax: thread i owns query row i (TMEM lane i); reads S_j,
-//               keeps (m, l) in log2 units, writes P_j (bf16, 128B-swizzled
-//               K-major) and, only when a row max grows by more than 2^8,
-//               rescales that warp's O rows in TMEM; finally normalises O and
-//               applies the per-head gate (2*sigmoid logits) in the epilogue.
-//   warps 2..3  idle (keep the softmax warps on TMEM lane quarters 0..3)
+// CTA = two 128-row query tiles (A, B) of one head sharing every K/V tile,
+// 320 threads:
+//   warps 0..3  softmax of tile A: thread i owns query row i (TMEM lane i)
+//   warps 4..7  softmax of tile B
+//   warp 8      TMA producer: Q_A, Q_B once, then K_j / V_j (128 x 128 bf16)
+//               into a 2-stage ring with separate K and V barriers
+//   warp 9      TMEM owner + single-thread tcgen05.mma issuer
+// TMEM (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
+// The softmax writes P_X (bf16 pairs) back over the first 64 columns of S_X,
+// and O_X += P_X V_j reads its A operand straight from TMEM.
 //
-// K/V rows past Tkv are zero-filled by TMA and masked to -inf before the
-// softmax; query rows past Tq are computed and dropped.
+// MMA issue order: S_A0 S_B0 | PV_A0 S_A1 | PV_B0 S_B1 | PV_A1 S_A2 | ...
+// so the softmax of one tile runs while the tensor core works on the other.
+// tcgen05 MMAs from one thread complete in order, so the commit that
+// signals S_X(j) also covers PV_X(j-1): once S_X(j) is visible, P_X(j-1)'s
+// columns and O_X are free to overwrite / rescale.
+//
+// Softmax per row: scores in log2 units, a running reference max that only
+// moves (with an O rescale in TMEM) when the tile max exceeds it by more than
+// 2^8, exp2 split between the MUFU unit and a degree-3 polynomial on the FMA
+// pipe, row sums in f32. K/V rows past Tkv are zero-filled by TMA and masked;
+// query rows past Tq are computed and dropped.
 //
 // Ring attention: with MERGE, the kernel processes one K/V shard and merges
 // its (m, l, O) into an f32 running state instead of writing the output.
@@ -29,38 +36,55 @@ constexpr int AT_BM = 128, AT_BN = 128, AT_D = 128;
 constexpr int AT_STAGES = 2;
 constexpr int AT_TILE = AT_BM * AT_D * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-col halves)
 constexpr int AT_HALF = AT_TILE / 2;
-constexpr int AT_SMEM = 1024 + AT_TILE /*Q*/ + 2 * AT_STAGES * AT_TILE /*K,V*/ + AT_TILE /*P*/ + 256;
+constexpr int AT_THREADS = 320;
+constexpr int AT_SMEM = 1024 + 2 * AT_TILE /*Q_A,Q_B*/ + 2 * AT_STAGES * AT_TILE /*K,V*/ + 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when the max grows by > 2^8
 
-__device__ __forceinline__ float ex2(float x) {
+__device__ __forceinline__ float ex2_mufu(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
+// 2^x on the FMA pipe: x = n + f with n = rint(x) (via the 1.5 * 2^23
+// rounding constant), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted by
+// least squares on Chebyshev nodes of [-1/2, 1/2] (max relative error
+// 7.8e-5); 2^n is added to the exponent field. x is clamped to >= -120, which
+// keeps the exponent arithmetic in range (2^-120 is negligible next to a
+// row sum >= 1).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -120.0f);
+  const float magic = 12582912.0f;  // 1.5 * 2^23
+  const float t = x + magic;
+  const float n = t - magic;
+  const float f = x - n;
+  float p = fmaf(0.05508868396282196f, f, 0.24260404706001282f);
+  p = fmaf(p, f, 0.6932762265205383f);
+  p = fmaf(p, f, 0.9999289512634277f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 template <bool MERGE>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(AT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + AT_TILE;
-  uint8_t* sV = sK + AT_STAGES * AT_TILE;
-  uint8_t* sP = sV + AT_STAGES * AT_TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + AT_TILE);
+  uint8_t* sQ = smem;                        // Q_A, Q_B
+  uint8_t* sK = sQ + 2 * AT_TILE;            // [stage]
+  uint8_t* sV = sK + AT_STAGES * AT_TILE;    // [stage]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + AT_STAGES * AT_TILE);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;              // [2]
-  uint64_t* v_full = bars + 3;              // [2]
-  uint64_t* kv_empty = bars + 5;            // [2]
-  uint64_t* s_full = bars + 7;              // [2]
-  uint64_t* s_free = bars + 9;              // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* pv_done = bars + 12;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* s_full = bars + 7;    // [tile]
+  uint64_t* p_full = bars + 9;    // [tile]
+  uint64_t* o_done = bars + 11;   // [tile]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
 
   const int warp = warp_id(), lane = lane_id();
-  const int q0 = blockIdx.x * AT_BM, h = blockIdx.y;
+  const int q0 = blockIdx.x * (2 * AT_BM), h = blockIdx.y;
   const int H = args.H, Tq = args.Tq, Tkv = args.Tkv;
   const int nkv = (Tkv + AT_BN - 1) / AT_BN;
   const int col0 = h * AT_D;
@@ -72,33 +96,33 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  if (warp == 9) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS0 = tmem, tO = tmem + 256;
 
-  if (warp == 0) {
+  if (warp == 8) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, AT_TILE);
+      mbar_arrive_expect_tx(q_full, 2 * AT_TILE);
       tma_load_2d(sQ, &tmQ, q_full, col0, q0);
       tma_load_2d(sQ + AT_HALF, &tmQ, q_full, col0 + 64, q0);
+      tma_load_2d(sQ + AT_TILE, &tmQ, q_full, col0, q0 + AT_BM);
+      tma_load_2d(sQ + AT_TILE + AT_HALF, &tmQ, q_full, col0 + 64, q0 + AT_BM);
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, 0x201)) goto done;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, 0x201)) goto done;
         uint8_t* k = sK + st * AT_TILE;
         uint8_t* v = sV + st * AT_TILE;
         mbar_arrive_expect_tx(&k_full[st], AT_TILE);
@@ -109,133 +133,170 @@ __global__ void __launch_bounds__(256, 1)
         tma_load_2d(v + AT_HALF, &tmV, &v_full[st], col0 + 64, j * AT_BN);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(AT_BM, AT_BN, 0, 0);
       constexpr uint32_t idesc_o = idesc_bf16_f32(AT_BM, AT_D, 0, 1);
       const uint32_t qa = smem_u32(sQ);
-      if (!mbar_wait(q_full, 0, 0x202)) goto done;
-      // S_0
-      if (!mbar_wait(&k_full[0], 0, 0x203)) goto done;
-      tc_fence_after();
-      {
-        const uint32_t ka = smem_u32(sK);
+      auto issue_s = [&](int tile, int j) {
+        const uint32_t ka = smem_u32(sK + (j & 1) * AT_TILE);
+        const uint32_t qt = qa + tile * AT_TILE;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * AT_HALF + (kk & 3) * 32;
-          umma_ss(tS0, sdesc_kmajor_sw128(qa + off), sdesc_kmajor_sw128(ka + off), idesc_s, kk > 0);
+          umma_ss(tmem + tile * 128, sdesc_kmajor_sw128(qt + off), sdesc_kmajor_sw128(ka + off), idesc_s, kk > 0);
         }
-        umma_commit(&s_full[0]);
-      }
+        umma_commit(&s_full[tile]);
+      };
+      auto issue_pv = [&](int tile, int j) {
+        const uint32_t va = smem_u32(sV + (j & 1) * AT_TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ts(tmem + 256 + tile * 128, tmem + tile * 128 + kk * 8, sdesc_mnmajor_sw128(va + kk * 2048, AT_HALF),
+                  idesc_o, (j | kk) != 0);
+      };
+      if (!mbar_wait(q_full, 0, 0x202)) goto done;
+      if (!mbar_wait(&k_full[0], 0, 0x203)) goto done;
+      tc_fence_after();
+      issue_s(0, 0);
+      issue_s(1, 0);
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
-        if (j + 1 < nkv) {
-          const int sn = (j + 1) & 1;
-          const uint32_t use = (uint32_t)((j + 1) >> 1);  // uses of S buffer sn so far
-          if (!mbar_wait(&s_free[sn], (use & 1) ^ 1, 0x204)) goto done;
-          if (!mbar_wait(&k_full[sn], ((j + 1) >> 1) & 1, 0x205)) goto done;
-          tc_fence_after();
-          const uint32_t ka = smem_u32(sK + sn * AT_TILE);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * AT_HALF + (kk & 3) * 32;
-            umma_ss(tS0 + sn * AT_BN, sdesc_kmajor_sw128(qa + off), sdesc_kmajor_sw128(ka + off), idesc_s, kk > 0);
-          }
-          umma_commit(&s_full[sn]);
-        }
-        if (!mbar_wait(p_full, j & 1, 0x206)) goto done;
-        if (!mbar_wait(&v_full[st], (j >> 1) & 1, 0x207)) goto done;
+        const bool more = j + 1 < nkv;
+        // tile A: O_A += P_A V_j, then S_A(j+1)
+        if (!mbar_wait(&p_full[0], j & 1, 0x204)) goto done;
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1, 0x205)) goto done;
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP), va = smem_u32(sV + st * AT_TILE);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t adesc = sdesc_kmajor_sw128(pa + (kk >> 2) * AT_HALF + (kk & 3) * 32);
-          const uint64_t bdesc = sdesc_mnmajor_sw128(va + kk * 2048, AT_HALF);
-          umma_ss(tO, adesc, bdesc, idesc_o, (j | kk) != 0);
+        issue_pv(0, j);
+        if (more) {
+          if (!mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1, 0x206)) goto done;
+          tc_fence_after();
+          issue_s(0, j + 1);
+        } else {
+          umma_commit(&o_done[0]);
         }
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[st]);
+        // tile B
+        if (!mbar_wait(&p_full[1], j & 1, 0x207)) goto done;
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&kv_empty[st]);  // K_j, V_j consumed by every MMA issued so far
+        if (more)
+          issue_s(1, j + 1);
+        else
+          umma_commit(&o_done[1]);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- softmax / correction / epilogue ----------------
+  } else {
+    // ---------------- softmax / correction / epilogue (warps 0..7) ----------------
+    const int tile = warp >> 2;  // 0 = A, 1 = B
     const int qw = warp & 3;
-    const int r = qw * 32 + lane;                  // row within the tile == TMEM lane
+    const int r = qw * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const uint32_t tS = tmem + tile * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + tile * 128 + lane_off;
     const float c = args.scale * 1.4426950408889634f;  // scores -> log2 units
-    float m_ref = -INFINITY, l = 0.f;
+    float m_ref = -INFINITY, l = 0.f;  // m_ref in log2 units
     bool ok = true;
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int sb = j & 1;
-      if (!warp_wait(&s_full[sb], (j >> 1) & 1, 0x208)) { ok = false; break; }
+    for (int j = 0; j < nkv; ++j) {
+      if (!warp_wait(&s_full[tile], j & 1, 0x208)) { ok = false; break; }
       tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t u[32];
-        tmem_ld32(tS0 + sb * AT_BN + lane_off + cc * 32, u);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[cc * 32 + e] = __uint_as_float(u[e]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
+      // One streaming pass over the 128 scores in four 32-column chunks (the
+      // next chunk's TMEM load overlaps this chunk's math). p = 2^(s c - m)
+      // uses the running reference max m; a chunk whose max exceeds m by more
+      // than 2^8 moves m up and rescales what this row already holds (l, the
+      // P chunks written this iteration, and O from earlier iterations).
+      // P chunk k (bf16 pairs) goes to columns [16k, 16k + 16), all of which
+      // were read before.
       const int valid = Tkv - j * AT_BN;  // columns < valid are real keys
-      float mx = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < 128; ++e) {
-        s[e] = (e < valid) ? s[e] * c : -INFINITY;
-        mx = fmaxf(mx, s[e]);
-      }
-      // previous P_{j-1} must be consumed (and O_{j-1} final) before we touch
-      // the P buffer or O
-      if (j > 0 && !warp_wait(pv_done, (j - 1) & 1, 0x209)) { ok = false; break; }
-      const bool need = mx > m_ref + kRescaleThreshold;
-      if (j == 0) {
-        m_ref = mx;
-      } else if (__any_sync(0xffffffffu, need)) {
-        const float m_new = need ? mx : m_ref;
-        const float corr = ex2(m_ref - m_new);
-        l *= corr;
-        m_ref = m_new;
-        tc_fence_after();
+      float sum = 0.f;
+      uint32_t cur[32], nxt[32];
+      tmem_ld32(tS, cur);
+      tmem_wait_ld();
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t u[32];
-          tmem_ld32(tO + lane_off + cc * 32, u);
+      for (int ch = 0; ch < 4; ++ch) {
+        if (ch < 3) tmem_ld32(tS + (ch + 1) * 32, nxt);
+        float v[32];  // raw scores; c > 0 so max(v) * c is the max in log2 units
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(cur[e]);
+        if (valid < AT_BN) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (ch * 32 + e >= valid) v[e] = -INFINITY;
+        }
+        float m4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+        for (int e = 4; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], v[e]);
+        const float cm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * c;
+        const bool need = cm > m_ref + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_new = need ? cm : m_ref;
+          const float corr = ex2_mufu(m_ref - m_new);  // 0 on the very first chunk
+          m_ref = m_new;
+          l *= corr;
+          sum *= corr;
+          if (ch > 0) {  // P chunks already written this iteration
+            tmem_wait_st();
+            uint32_t pp[32];
+            tmem_ld32(tS, pp);  // columns [0, 32) hold P chunks 0 and 1
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (e < 16 * ch) pp[e] = pack_bf16x2(bf16_lo(pp[e]) * corr, bf16_hi(pp[e]) * corr);
+            tmem_st32(tS, pp);
+            if (ch > 2) {
+              uint32_t p3[16];
+              // chunk 2's P lives in [32, 48): reload, scale, store
+              uint32_t q32[32];
+              tmem_ld32(tS + 32, q32);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) p3[e] = pack_bf16x2(bf16_lo(q32[e]) * corr, bf16_hi(q32[e]) * corr);
+              tmem_st16(tS + 32, p3);
+            }
+          }
+          if (j > 0) {  // O from earlier iterations (complete: S(j) committed after PV(j-1))
+#pragma unroll 1
+            for (int cc = 0; cc < 4; ++cc) {
+              uint32_t u[32];
+              tmem_ld32(tO + cc * 32, u);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
+              tmem_st32(tO + cc * 32, u);
+            }
+          }
+        }
+        const float mc = m_ref;
+        uint32_t pk[16];
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          // 3 of every 8 exponentials on the FMA pipe, the rest on MUFU
+          const float a0 = fmaf(v[2 * e], c, -mc), a1 = fmaf(v[2 * e + 1], c, -mc);
+          const float p0 = ((e & 3) == 1) ? ex2_poly(a0) : ex2_mufu(a0);
+          const float p1 = ((e & 1) == 1) ? ex2_poly(a1) : ex2_mufu(a1);
+          s4[e & 3] += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        tmem_st16(tS + ch * 16, pk);
+        if (ch < 3) {
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
-          tmem_st32(tO + lane_off + cc * 32, u);
+          for (int e = 0; e < 32; ++e) cur[e] = nxt[e];
         }
-        tmem_wait_st();
-      }
-      float sum = 0.f;
-      uint8_t* prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2(s[ch * 8 + 2 * e] - m_ref);
-          const float p1 = ex2(s[ch * 8 + 2 * e + 1] - m_ref);
-          sum += p0 + p1;
-          w[e] = pack_bf16x2(p0, p1);
-        }
-        const int half = ch >> 3, lc = ch & 7;
-        *reinterpret_cast<uint4*>(prow + half * AT_HALF + ((lc ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l += sum;
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[tile]);
     }
     // ---------------- epilogue ----------------
-    if (ok && warp_wait(pv_done, (nkv - 1) & 1, 0x20A)) {
+    if (ok && warp_wait(&o_done[tile], 0, 0x209)) {
       tc_fence_after();
-      const int row = q0 + r;
+      const int row = q0 + tile * AT_BM + r;
       const bool row_ok = row < Tq;
       const size_t obase = ((size_t)row * H + h) * AT_D;
       if (!MERGE) {
@@ -244,7 +305,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll 1
         for (int cc = 0; cc < 4; ++cc) {
           uint32_t u[32];
-          tmem_ld32(tO + lane_off + cc * 32, u);
+          tmem_ld32(tO + cc * 32, u);
           tmem_wait_ld();
           if (row_ok) {
             uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) + obase + cc * 32);
@@ -267,8 +328,8 @@ __global__ void __launch_bounds__(256, 1)
           } else {
             const float ms = args.m_state[si], ls = args.l_state[si];
             const float mn = fmaxf(ms, m_ref);
-            a = ex2(ms - mn);
-            b = ex2(m_ref - mn);
+            a = ex2_mufu(ms - mn);
+            b = ex2_mufu(m_ref - mn);
             args.m_state[si] = mn;
             args.l_state[si] = ls * a + l * b;
           }
@@ -276,7 +337,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll 1
         for (int cc = 0; cc < 4; ++cc) {
           uint32_t u[32];
-          tmem_ld32(tO + lane_off + cc * 32, u);
+          tmem_ld32(tO + cc * 32, u);
           tmem_wait_ld();
           if (row_ok) {
             float4* op = reinterpret_cast<float4*>(args.o_acc + obase + cc * 32);
@@ -301,7 +362,7 @@ __global__ void __launch_bounds__(256, 1)
 done:
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -341,8 +402,9 @@ static int launch_attn(const AttnArgs& a, cudaStream_t st) {
   if (!rc) rc = make_tmap_2d(&tk, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, a.Tkv, a.ldk, 64, AT_BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = make_tmap_2d(&tv, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, a.Tkv, a.ldv, 64, AT_BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  dim3 grid((a.Tq + AT_BM - 1) / AT_BM, a.H);
-  attn_tc_kernel<MERGE><<<grid, 256, AT_SMEM, st>>>(tq, tk, tv, a);
+  dim3 grid((a.Tq + 2 * AT_BM - 1) / (2 * AT_BM), a.H);
+  attn_tc_kernel<MERGE><<<grid, AT_THREADS, AT_SMEM, st>>>(tq, tk, tv, a);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "attention launch");
 }
@@ -365,6 +427,7 @@ int attention_finalize(const AttnArgs& a, cudaStream_t st) {
   if (grid > 8 * sm_count()) grid = 8 * sm_count();
   attn_finalize_kernel<<<grid, 256, 0, st>>>(a.o_acc, a.l_state, a.gate, a.ldg, a.Tq, a.H,
                                              reinterpret_cast<__nv_bfloat16*>(a.out));
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "attention finalize");
 }

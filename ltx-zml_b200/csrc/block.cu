@@ -453,9 +453,15 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   // 1. n = modulate(rms(x), ada1, ada0)
   if (stage == LTXB_STAGE_S1_NORM_MSA)
     return norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, 0, 1, stage_out, 1, nullptr, st);
-  CK(norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, 0, 1, b.n, f32, nullptr, st));
+  {
+    Phase p("norm_msa", st);
+    CK(norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, 0, 1, b.n, f32, nullptr, st));
+  }
   // 2. fused q/k/v projection (+ q/k sums of squares)
-  CK(run_lin(lc, w->qkv1, b.n, D, T, f32 ? EPI_F32 : EPI_BF16_SSQ, b.qkv, 3 * D, b.ssq, 2 * D));
+  {
+    Phase p("gemm_qkv1", st);
+    CK(run_lin(lc, w->qkv1, b.n, D, T, f32 ? EPI_F32 : EPI_BF16_SSQ, b.qkv, 3 * D, b.ssq, 2 * D));
+  }
   const int n_ssq = D / 256;  // N tiles per q (or k) part at BN = 256
   if (stage == LTXB_STAGE_S1B_QNORM) {
     if (f32) return qk_norm_rope_f32(static_cast<const float*>(b.qkv), 3 * D, w->qn1, nullptr, nullptr, T, D, stage_out, st);
@@ -463,9 +469,14 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   }
   // 3. gate logits
   const bool gated = stage != LTXB_STAGE_S2_ATTN1_NOGATE;
-  if (gated) CK(run_lin(lc, w->g1, b.n, D, T, EPI_GATE2SIG_F32, b.gate, w->G));
+  if (gated) {
+    Phase p("gemm_gate1", st);
+    CK(run_lin(lc, w->g1, b.n, D, T, EPI_GATE2SIG_F32, b.gate, w->G));
+  }
   // 4. q/k norm + RoPE (K goes to its slot of the gathered buffer under SP)
   void* k_dst = col(b.k, (size_t)(sp ? c->sp_rank : 0) * T * D);
+  {
+  Phase p("qk_norm_rope", st);
   if (f32) {
     CK(qk_norm_rope_f32(static_cast<const float*>(b.qkv), 3 * D, w->qn1, io->cos, io->sin, T, D,
                         static_cast<float*>(b.q), st));
@@ -475,31 +486,52 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
     CK(qk_norm_rope2(b.qkv, col(b.qkv, D), 3 * D, b.ssq, b.ssq + n_ssq, 32, n_ssq, w->qn1, w->kn1, io->cos, io->sin,
                      T, D, b.q, k_dst, st));
   }
+  }
   // 5. self-attention
   const float* g1 = gated ? b.gate : nullptr;
-  if (sp)
-    CK(ring_attention(w, c, b, b.q, col(b.qkv, 2 * D), 3 * D, g1, st));
-  else
-    CK(attn(w, b.q, D, b.k, D, col(b.qkv, 2 * D), 3 * D, b.o, g1, T, T, st));
+  {
+    Phase p("attn_self", st);
+    if (sp)
+      CK(ring_attention(w, c, b, b.q, col(b.qkv, 2 * D), 3 * D, g1, st));
+    else
+      CK(attn(w, b.q, D, b.k, D, col(b.qkv, 2 * D), 3 * D, b.o, g1, T, T, st));
+  }
   if (stage == LTXB_STAGE_S2_ATTN1_NOGATE || stage == LTXB_STAGE_S3_ATTN1)
     return run_lin(lc, w->o1, b.o, D, T, EPI_F32, stage_out, D);
   // 6. x_sa = x + (o Wo^T + bo) * ada2
-  CK(run_lin(lc, w->o1, b.o, D, T, EPI_RESID_F32, b.x_sa, D, nullptr, 0, io->x, io->tstab, io->tidx, 2));
+  {
+    Phase p("gemm_o1", st);
+    CK(run_lin(lc, w->o1, b.o, D, T, EPI_RESID_F32, b.x_sa, D, nullptr, 0, io->x, io->tstab, io->tidx, 2));
+  }
   if (stage == LTXB_STAGE_S4_AFTER_SA)
     return cudaMemcpyAsync(stage_out, b.x_sa, (size_t)T * D * 4, cudaMemcpyDeviceToDevice, st) == cudaSuccess
                ? LTXB_OK
                : set_error(LTXB_ECUDA, "stage copy");
   if (stage == LTXB_STAGE_S4_NORMED) return rms_rows(b.x_sa, T, D, stage_out, st);
   // 7. cross-attention query input
-  CK(norm_modulate(b.x_sa, T, D, w->sst, io->tstab, io->tidx, 6, 7, b.n, f32, nullptr, st));
+  {
+    Phase p("norm_ca", st);
+    CK(norm_modulate(b.x_sa, T, D, w->sst, io->tstab, io->tidx, 6, 7, b.n, f32, nullptr, st));
+  }
   // 8. prompt K/V
-  CK(ctx_modulate(io->ctx, S, D, w->psst, io->pts2, f32 ? nullptr : b.enc, f32 ? static_cast<float*>(b.enc) : nullptr,
-                  st));
-  CK(run_lin(lc, w->kv2, b.enc, D, S, f32 ? EPI_F32 : EPI_BF16_SSQ, b.kv2, 2 * D, b.ssq2, D));
+  {
+    Phase p("prompt_kv", st);
+    CK(ctx_modulate(io->ctx, S, D, w->psst, io->pts2, f32 ? nullptr : b.enc,
+                    f32 ? static_cast<float*>(b.enc) : nullptr, st));
+    CK(run_lin(lc, w->kv2, b.enc, D, S, f32 ? EPI_F32 : EPI_BF16_SSQ, b.kv2, 2 * D, b.ssq2, D));
+  }
   // 9. q2 and gate2
-  CK(run_lin(lc, w->q2, b.n, D, T, f32 ? EPI_F32 : EPI_BF16_SSQ, b.qkv, D, b.ssq, D));
-  CK(run_lin(lc, w->g2, b.n, D, T, EPI_GATE2SIG_F32, b.gate, w->G));
+  {
+    Phase p("gemm_q2", st);
+    CK(run_lin(lc, w->q2, b.n, D, T, f32 ? EPI_F32 : EPI_BF16_SSQ, b.qkv, D, b.ssq, D));
+  }
+  {
+    Phase p("gemm_gate2", st);
+    CK(run_lin(lc, w->g2, b.n, D, T, EPI_GATE2SIG_F32, b.gate, w->G));
+  }
   // 10. q2 / k2 norms (no RoPE in cross-attention, ltx/block.zig:304)
+  {
+  Phase p("qk_norm2", st);
   if (f32) {
     CK(qk_norm_rope_f32(static_cast<const float*>(b.qkv), D, w->qn2, nullptr, nullptr, T, D, static_cast<float*>(b.q), st));
     CK(qk_norm_rope_f32(static_cast<const float*>(b.kv2), 2 * D, w->kn2, nullptr, nullptr, S, D,
@@ -508,21 +540,37 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
     CK(qk_norm_rope(b.qkv, D, b.ssq, 32, n_ssq, w->qn2, nullptr, nullptr, T, D, b.q, nullptr, st));
     CK(qk_norm_rope(b.kv2, 2 * D, b.ssq2, 32, n_ssq, w->kn2, nullptr, nullptr, S, D, b.k2, nullptr, st));
   }
+  }
   // 11. cross-attention
-  CK(attn(w, b.q, D, b.k2, D, col(b.kv2, D), 2 * D, b.o, b.gate, T, S, st));
+  {
+    Phase p("attn_cross", st);
+    CK(attn(w, b.q, D, b.k2, D, col(b.kv2, D), 2 * D, b.o, b.gate, T, S, st));
+  }
   // 12. x_ca = x_sa + (o2 Wo2^T + b) * ada8
   if (stage == LTXB_STAGE_S5_CA_OUT)
     return run_lin(lc, w->o2, b.o, D, T, EPI_RESID_F32, stage_out, D, nullptr, 0, nullptr, io->tstab, io->tidx, 8);
-  CK(run_lin(lc, w->o2, b.o, D, T, EPI_RESID_F32, b.x_ca, D, nullptr, 0, b.x_sa, io->tstab, io->tidx, 8));
+  {
+    Phase p("gemm_o2", st);
+    CK(run_lin(lc, w->o2, b.o, D, T, EPI_RESID_F32, b.x_ca, D, nullptr, 0, b.x_sa, io->tstab, io->tidx, 8));
+  }
   // 13. FFN input
   if (stage == LTXB_STAGE_S6_FF_IN)
     return norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, 3, 4, stage_out, 1, nullptr, st);
-  CK(norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, 3, 4, b.n, f32, nullptr, st));
+  {
+    Phase p("norm_mlp", st);
+    CK(norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, 3, 4, b.n, f32, nullptr, st));
+  }
   // 14. h = gelu(f W1^T)
-  CK(run_lin(lc, w->ff1, b.n, D, T, EPI_GELU_BF16, b.h, FF));
+  {
+    Phase p("gemm_ff1", st);
+    CK(run_lin(lc, w->ff1, b.n, D, T, EPI_GELU_BF16, b.h, FF));
+  }
   // 15. out = x_ca + (h W2^T) * ada5
   if (stage == LTXB_STAGE_S7_FF_OUT) return run_lin(lc, w->ff2, b.h, FF, T, EPI_F32, stage_out, D);
-  CK(run_lin(lc, w->ff2, b.h, FF, T, EPI_RESID_F32, io->out, D, nullptr, 0, b.x_ca, io->tstab, io->tidx, 5));
+  {
+    Phase p("gemm_ff2", st);
+    CK(run_lin(lc, w->ff2, b.h, FF, T, EPI_RESID_F32, io->out, D, nullptr, 0, b.x_ca, io->tstab, io->tidx, 5));
+  }
 #undef CK
   return LTXB_OK;
 }

@@ -92,6 +92,7 @@ int norm_modulate(const float* x, int T, int D, const float* sst, const float* t
   if (T <= 0) return LTXB_OK;
   if (D % 4) return set_error(LTXB_EINVAL, "norm_modulate: D %% 4");
   norm_modulate_kernel<<<T, ROW_THREADS, 0, st>>>(x, D, sst, tstab, tidx, r_shift, r_scale, out, out_f32, rms_copy);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "norm_modulate");
 }
@@ -201,6 +202,7 @@ int qk_norm_rope(const void* raw, int ld_raw, const float* ssq, int ssq_ld, int 
   QkSide s{reinterpret_cast<const __nv_bfloat16*>(raw), ld_raw, ssq, ssq_ld,
            reinterpret_cast<const __nv_bfloat16*>(w_bf16), reinterpret_cast<__nv_bfloat16*>(out_bf16), out_f32};
   qk_norm_rope_kernel<<<T, ROW_THREADS, 0, st>>>(s, s, 1, n_ssq, cos, sin, D);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "qk_norm_rope");
 }
@@ -215,6 +217,7 @@ int qk_norm_rope2(const void* raw_q, const void* raw_k, int ld_raw, const float*
   QkSide b{reinterpret_cast<const __nv_bfloat16*>(raw_k), ld_raw, ssq_k, ssq_ld,
            reinterpret_cast<const __nv_bfloat16*>(wk), reinterpret_cast<__nv_bfloat16*>(out_k), nullptr};
   qk_norm_rope_kernel<<<T, ROW_THREADS, 0, st>>>(a, b, 2, n_ssq, cos, sin, D);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "qk_norm_rope2");
 }
@@ -260,6 +263,7 @@ int qk_norm_rope_f32(const float* raw, int ld_raw, const void* w_bf16, const flo
   if (T <= 0) return LTXB_OK;
   qk_norm_rope_f32_kernel<<<T, ROW_THREADS, 0, st>>>(raw, ld_raw, reinterpret_cast<const __nv_bfloat16*>(w_bf16),
                                                      cos, sin, D, out);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "qk_norm_rope_f32");
 }
@@ -287,6 +291,7 @@ int ctx_modulate(const float* ctx, int S, int D, const float* psst, const float*
   if (grid > 4 * sm_count()) grid = 4 * sm_count();
   ctx_modulate_kernel<<<grid, 256, 0, st>>>(ctx, S, D, psst, pts2, reinterpret_cast<__nv_bfloat16*>(out_bf16),
                                             out_f32);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "ctx_modulate");
 }
@@ -326,6 +331,7 @@ int dequant_weights(const int8_t* q, const void* scales, int scale_bf16, int N, 
   int grid = (int)((n16 + 255) / 256);
   if (grid > 8 * sm_count()) grid = 8 * sm_count();
   dequant_weights_kernel<<<grid, 256, 0, st>>>(q, scales, scale_bf16, N, K, reinterpret_cast<__nv_bfloat16*>(out));
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "dequant_weights");
 }
@@ -343,6 +349,7 @@ int cast_f32_bf16(const float* in, void* out, size_t n, cudaStream_t st) {
   int grid = (int)((n / 4 + 255) / 256);
   if (grid > 8 * sm_count()) grid = 8 * sm_count();
   cast_f32_bf16_kernel<<<grid, 256, 0, st>>>(in, reinterpret_cast<__nv_bfloat16*>(out), n);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "cast_f32_bf16");
 }
@@ -357,6 +364,7 @@ int cast_bf16_f32(const void* in, float* out, size_t n, cudaStream_t st) {
   int grid = (int)((n + 255) / 256);
   if (grid > 8 * sm_count()) grid = 8 * sm_count();
   cast_bf16_f32_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(in), out, n);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "cast_bf16_f32");
 }

@@ -95,6 +95,7 @@ int gemm_f32(const float* A, int lda, const void* W, int M, int N, int K, const 
   gemm_f32_kernel<<<grid, 256, 0, st>>>(A, lda, reinterpret_cast<const __nv_bfloat16*>(W), M, N, K,
                                         reinterpret_cast<const __nv_bfloat16*>(bias), epi, out, ldo, xres, sst, tstab,
                                         tidx, ada_row);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "gemm_f32");
 }
@@ -234,6 +235,7 @@ int attention_f32(const float* q, int ldq, const float* k, int ldk, const float*
   }
   dim3 grid((Tq + FA_Q - 1) / FA_Q, H);
   attention_f32_kernel<<<grid, 256, smem, st>>>(q, ldq, k, ldk, v, ldv, out, gate, ldg, Tq, Tkv, H, scale);
+  launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "attention_f32");
 }

@@ -334,6 +334,7 @@ static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
   const int num_tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * (a.N / BN);
   const int grid = num_tiles < sm_count() ? num_tiles : sm_count();
   kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, a);
+  launched();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "gemm launch");
   return LTXB_OK;

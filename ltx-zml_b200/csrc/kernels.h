@@ -15,6 +15,20 @@ int set_error(int code, const char* fmt, ...);
 int set_cuda_error(cudaError_t e, const char* what);
 int sm_count();
 
+// ---- launch accounting and per-phase profiling ----
+// Every kernel launcher calls launched() after a successful launch, so
+// ltxb_launch_count() counts this library's kernels.
+void launched();
+// RAII phase marker: with profiling on, records CUDA events on `st` around
+// the scope and attributes the elapsed device time to `name`.
+struct Phase {
+  Phase(const char* name, cudaStream_t st);
+  ~Phase();
+  const char* name;
+  cudaStream_t st;
+  int slot;
+};
+
 // ---- TMA descriptors ----
 // 2-D tensor map of a row-major [rows, cols] matrix with row stride `ld`
 // elements; box [box_rows, box_cols]. x = column (innermost), y = row.

@@ -6,7 +6,10 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
+#include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -41,6 +44,57 @@ int sm_count() {
     g_sms[dev] = n;
   }
   return g_sms[dev];
+}
+
+// ---- launch accounting / profiling ----
+static std::atomic<uint64_t> g_launches{0};
+void launched() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+namespace {
+struct ProfRec {
+  std::string name;
+  cudaEvent_t a, b;
+  uint64_t launches;
+};
+struct ProfState {
+  std::mutex mu;
+  bool on = false;
+  std::vector<cudaEvent_t> pool;
+  std::vector<ProfRec> pending;
+  std::vector<std::string> names;
+  std::vector<double> ms;
+  std::vector<uint64_t> launches;
+  std::vector<int> count;
+};
+ProfState g_prof;
+
+cudaEvent_t prof_event() {
+  if (!g_prof.pool.empty()) {
+    cudaEvent_t e = g_prof.pool.back();
+    g_prof.pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+}  // namespace
+
+Phase::Phase(const char* n, cudaStream_t s) : name(n), st(s), slot(-1) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  if (!g_prof.on) return;
+  ProfRec r{n, prof_event(), prof_event(), g_launches.load()};
+  cudaEventRecord(r.a, st);
+  g_prof.pending.push_back(r);
+  slot = (int)g_prof.pending.size() - 1;
+}
+
+Phase::~Phase() {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  if (slot < 0 || slot >= (int)g_prof.pending.size()) return;
+  ProfRec& r = g_prof.pending[slot];
+  cudaEventRecord(r.b, st);
+  r.launches = g_launches.load() - r.launches;
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -99,6 +153,53 @@ int ltxb_init(int device) {
                      p.minor);
   sm_count();
   return resolve_encoder();
+}
+
+uint64_t ltxb_launch_count(void) { return g_launches.load(); }
+
+int ltxb_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  g_prof.on = on != 0;
+  return LTXB_OK;
+}
+
+int ltxb_profile_collect(int max_phases, char* names, int name_stride, double* total_ms, uint64_t* launches,
+                         int* calls, int reset) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  for (ProfRec& r : g_prof.pending) {
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(r.b);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, r.a, r.b);
+    if (e != cudaSuccess) return set_cuda_error(e, "profile events");
+    size_t i = 0;
+    while (i < g_prof.names.size() && g_prof.names[i] != r.name) ++i;
+    if (i == g_prof.names.size()) {
+      g_prof.names.push_back(r.name);
+      g_prof.ms.push_back(0.0);
+      g_prof.launches.push_back(0);
+      g_prof.count.push_back(0);
+    }
+    g_prof.ms[i] += ms;
+    g_prof.launches[i] += r.launches;
+    g_prof.count[i] += 1;
+    g_prof.pool.push_back(r.a);
+    g_prof.pool.push_back(r.b);
+  }
+  g_prof.pending.clear();
+  const int n = (int)g_prof.names.size();
+  for (int i = 0; i < n && i < max_phases; ++i) {
+    if (names && name_stride > 0) snprintf(names + (size_t)i * name_stride, name_stride, "%s", g_prof.names[i].c_str());
+    if (total_ms) total_ms[i] = g_prof.ms[i];
+    if (launches) launches[i] = g_prof.launches[i];
+    if (calls) calls[i] = g_prof.count[i];
+  }
+  if (reset) {
+    g_prof.names.clear();
+    g_prof.ms.clear();
+    g_prof.launches.clear();
+    g_prof.count.clear();
+  }
+  return n;
 }
 
 int ltxb_device_status(int clear, uint32_t* site) {

@@ -60,6 +60,9 @@ def _load() -> ctypes.CDLL:
         "ltxb_last_error": (ctypes.c_char_p, []),
         "ltxb_version": (ctypes.c_char_p, []),
         "ltxb_device_status": (i32, [i32, ctypes.POINTER(ctypes.c_uint32)]),
+        "ltxb_launch_count": (u64, []),
+        "ltxb_profile_enable": (i32, [i32]),
+        "ltxb_profile_collect": (i32, [i32, vp, i32, vp, vp, vp, i32]),
         "ltxb_blob_check_layout": (i32, [vp, i32, u64, ctypes.c_uint32]),
         "ltxb_weights_upload": (i32, [i32, vp, u64, vp, i32, i32, i32, i32, i32, i32, ctypes.POINTER(vp)]),
         "ltxb_weights_bytes": (u64, [vp]),
@@ -102,6 +105,32 @@ def device_status(clear: bool = True) -> int:
     """LTXB_OK or LTXB_ETIMEOUT (a bounded device wait expired). Syncs the device."""
     site = ctypes.c_uint32(0)
     return lib.ltxb_device_status(int(clear), ctypes.byref(site))
+
+
+def launch_count() -> int:
+    """Kernels libltxb.so has launched in this process."""
+    return int(lib.ltxb_launch_count())
+
+
+def profile_enable(on: bool = True) -> None:
+    _check(lib.ltxb_profile_enable(int(on)))
+
+
+def profile_collect(reset: bool = True) -> dict:
+    """{phase: (total_ms, launches, calls)} accumulated since the last reset."""
+    n = 64
+    names = ctypes.create_string_buffer(n * 32)
+    ms = (ctypes.c_double * n)()
+    la = (ctypes.c_uint64 * n)()
+    calls = (ctypes.c_int * n)()
+    k = lib.ltxb_profile_collect(n, names, 32, ms, la, calls, int(reset))
+    if k < 0:
+        _check(k)
+    out = {}
+    for i in range(min(k, n)):
+        nm = names.raw[i * 32:(i + 1) * 32].split(b"\0", 1)[0].decode()
+        out[nm] = (ms[i], int(la[i]), calls[i])
+    return out
 
 
 def _ptr(t) -> int | None:
