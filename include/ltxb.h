@@ -160,6 +160,14 @@ int ltxb_comm_get_id(void* id);
 int ltxb_comm_init(const void* id, int rank, int nranks, int device, ltxb_comm** out);
 void ltxb_comm_free(ltxb_comm* c);
 
+/* Ring schedule of the sequence-parallel self-attention (host-side, no GPU):
+ * at step s (0 <= s < nranks) rank r computes against K/V shard
+ * *compute_shard while sending that shard to *next_rank and receiving
+ * *recv_shard from *prev_rank (recv_shard = -1 on the last step). Shard i
+ * holds tokens [i T, (i+1) T). Pure function; the block's ring follows it. */
+int ltxb_ring_step(int rank, int nranks, int step, int* compute_shard, int* recv_shard, int* next_rank,
+                   int* prev_rank);
+
 /* ---- the block (ltx/block.zig:340-353, :544-574) ----------------------- */
 
 typedef struct {
@@ -206,6 +214,34 @@ int ltxb_block_forward(const ltxb_weights* w, const ltxb_block_io* io, const ltx
  * Single rank only. */
 int ltxb_block_stage(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_config* cfg, int stage,
                      float* stage_out, void* stream);
+
+/* ---- host-buffer pipeline ---------------------------------------------- */
+
+/* For callers whose activations live in host memory (the reference uploads
+ * x from the host with zml.Buffer.fromBytes and reads the block output back
+ * with toSliceAlloc, ltx/e2e_prod.zig:377-395): a pipe owns two device
+ * staging pairs (x, out) and two copy streams, so consecutive
+ * ltxb_block_forward_host calls overlap the host->device copy of call k and
+ * the device->host copy of call k-1 with the compute of call k. Every call
+ * still copies its whole input in and its whole result out. */
+typedef struct ltxb_host_pipe ltxb_host_pipe;
+
+/* `tables` supplies the per-call device tensors other than x/out (tstab,
+ * tidx, ctx, pts2, cos, sin) and the workspace; they must outlive the pipe.
+ * The pipe allocates 4 * T * D * 4 bytes of staging memory. */
+int ltxb_host_pipe_create(const ltxb_weights* w, const ltxb_config* cfg, const ltxb_block_io* tables,
+                          ltxb_host_pipe** out);
+
+/* Enqueue one block call: x_host [T, D] f32 -> out_host [T, D] f32 (pinned
+ * host memory gives full copy bandwidth). Compute runs on `stream`. x_host
+ * must stay unchanged and out_host unread until ltxb_host_pipe_join(). */
+int ltxb_block_forward_host(ltxb_host_pipe* p, const float* x_host, float* out_host, void* stream);
+
+/* Make `stream` wait for every copy the pipe has enqueued, so synchronising
+ * `stream` (or an event recorded on it afterwards) covers all results. */
+int ltxb_host_pipe_join(ltxb_host_pipe* p, void* stream);
+
+void ltxb_host_pipe_free(ltxb_host_pipe* p);
 
 /* ---- standalone operators (BASELINE configs 1 and 2) ------------------- */
 

@@ -360,6 +360,19 @@ static int attn(const ltxb_weights* w, const void* q, int ldq, const void* k, in
   return attention_tc(a, st);
 }
 
+struct RingStep {
+  int compute, recv, next, prev;
+};
+
+static RingStep ring_step(int r, int N, int s) {
+  RingStep x;
+  x.compute = ((r - s) % N + N) % N;
+  x.recv = (s + 1 < N) ? ((r - s - 1) % N + N) % N : -1;
+  x.next = (r + 1) % N;
+  x.prev = (r - 1 + N) % N;
+  return x;
+}
+
 // sequence-parallel self-attention: ring of K/V shards over NCCL, merging
 // (m, l, O) per shard; compute of shard s overlaps the receive of shard s+1.
 static int ring_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* v_local,
@@ -377,7 +390,6 @@ static int ring_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, 
   // comm stream starts after this rank's K/V are ready
   cudaEventRecord(cm->ev[0], st);
   cudaStreamWaitEvent(cm->comm_stream, cm->ev[0], 0);
-  const int next = (r + 1) % N, prev = (r - 1 + N) % N;
   AttnArgs a{};
   a.q = q;
   a.ldq = D;
@@ -394,14 +406,15 @@ static int ring_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, 
   a.l_state = b.l_st;
   a.out = b.o;
   for (int s = 0; s < N; ++s) {
-    const int cur = ((r - s) % N + N) % N;   // shard held at step s
-    const int nxt = ((r - s - 1) % N + N) % N;  // shard arriving during step s
+    const RingStep rs = ring_step(r, N, s);
+    const int cur = rs.compute;  // shard held at step s
+    const int nxt = rs.recv;     // shard arriving during step s
     if (s + 1 < N) {
       ncclGroupStart();
-      ncclSend(kb + (size_t)cur * chunk, chunk, ncclUint8, next, cm->nccl, cm->comm_stream);
-      ncclRecv(kb + (size_t)nxt * chunk, chunk, ncclUint8, prev, cm->nccl, cm->comm_stream);
-      ncclSend(vb + (size_t)cur * chunk, chunk, ncclUint8, next, cm->nccl, cm->comm_stream);
-      ncclRecv(vb + (size_t)nxt * chunk, chunk, ncclUint8, prev, cm->nccl, cm->comm_stream);
+      ncclSend(kb + (size_t)cur * chunk, chunk, ncclUint8, rs.next, cm->nccl, cm->comm_stream);
+      ncclRecv(kb + (size_t)nxt * chunk, chunk, ncclUint8, rs.prev, cm->nccl, cm->comm_stream);
+      ncclSend(vb + (size_t)cur * chunk, chunk, ncclUint8, rs.next, cm->nccl, cm->comm_stream);
+      ncclRecv(vb + (size_t)nxt * chunk, chunk, ncclUint8, rs.prev, cm->nccl, cm->comm_stream);
       ncclResult_t nr = ncclGroupEnd();
       if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "ring step %d: %s", s, ncclGetErrorString(nr));
       cudaEventRecord(cm->ev[1 + s], cm->comm_stream);
@@ -581,6 +594,18 @@ using namespace ltxb;
 
 extern "C" {
 
+int ltxb_ring_step(int rank, int nranks, int step, int* compute_shard, int* recv_shard, int* next_rank,
+                   int* prev_rank) {
+  if (nranks < 1 || rank < 0 || rank >= nranks || step < 0 || step >= nranks)
+    return set_error(LTXB_EINVAL, "ring step: rank %d / %d, step %d", rank, nranks, step);
+  const RingStep x = ring_step(rank, nranks, step);
+  if (compute_shard) *compute_shard = x.compute;
+  if (recv_shard) *recv_shard = x.recv;
+  if (next_rank) *next_rank = x.next;
+  if (prev_rank) *prev_rank = x.prev;
+  return LTXB_OK;
+}
+
 int ltxb_blob_check_layout(const ltxb_entry* entries, int n_entries, uint64_t blob_bytes, uint32_t align) {
   if (n_entries < 0 || (n_entries > 0 && !entries) || align == 0) return set_error(LTXB_EINVAL, "bad arguments");
   uint64_t end = 0;
@@ -680,6 +705,119 @@ int ltxb_block_stage(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
     return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "stage copy");
   }
   return run_block(w, io, cfg, stage, stage_out, static_cast<cudaStream_t>(stream));
+}
+
+// ---- host-buffer pipeline ----
+}  // extern "C"
+
+struct ltxb_host_pipe {
+  const ltxb_weights* w = nullptr;
+  ltxb_config cfg{};
+  ltxb_block_io io{};
+  int device = 0;
+  size_t bytes = 0;
+  float* x_dev[2] = {nullptr, nullptr};
+  float* out_dev[2] = {nullptr, nullptr};
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t h2d_done[2] = {}, comp_done[2] = {}, d2h_done[2] = {}, start = nullptr;
+  int64_t calls = 0;
+  bool fresh = true;
+};
+
+extern "C" {
+
+void ltxb_host_pipe_free(ltxb_host_pipe* p) {
+  if (!p) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(p->device);
+  if (p->h2d) cudaStreamSynchronize(p->h2d);
+  if (p->d2h) cudaStreamSynchronize(p->d2h);
+  for (int i = 0; i < 2; ++i) {
+    if (p->x_dev[i]) cudaFree(p->x_dev[i]);
+    if (p->out_dev[i]) cudaFree(p->out_dev[i]);
+    if (p->h2d_done[i]) cudaEventDestroy(p->h2d_done[i]);
+    if (p->comp_done[i]) cudaEventDestroy(p->comp_done[i]);
+    if (p->d2h_done[i]) cudaEventDestroy(p->d2h_done[i]);
+  }
+  if (p->start) cudaEventDestroy(p->start);
+  if (p->h2d) cudaStreamDestroy(p->h2d);
+  if (p->d2h) cudaStreamDestroy(p->d2h);
+  cudaSetDevice(prev);
+  delete p;
+}
+
+int ltxb_host_pipe_create(const ltxb_weights* w, const ltxb_config* cfg, const ltxb_block_io* tables,
+                          ltxb_host_pipe** out) {
+  if (!out) return set_error(LTXB_EINVAL, "out is null");
+  *out = nullptr;
+  if (!w || !cfg || !tables) return set_error(LTXB_EINVAL, "null argument");
+  if (cfg->T <= 0) return set_error(LTXB_EINVAL, "T must be positive");
+  auto* p = new ltxb_host_pipe();
+  p->w = w;
+  p->cfg = *cfg;
+  p->io = *tables;
+  p->device = w->device;
+  p->bytes = (size_t)cfg->T * w->D * sizeof(float);
+  cudaSetDevice(w->device);
+  bool ok = true;
+  for (int i = 0; i < 2 && ok; ++i) {
+    ok = cudaMalloc(&p->x_dev[i], p->bytes) == cudaSuccess && cudaMalloc(&p->out_dev[i], p->bytes) == cudaSuccess &&
+         cudaEventCreateWithFlags(&p->h2d_done[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&p->comp_done[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&p->d2h_done[i], cudaEventDisableTiming) == cudaSuccess;
+  }
+  ok = ok && cudaEventCreateWithFlags(&p->start, cudaEventDisableTiming) == cudaSuccess &&
+       cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking) == cudaSuccess &&
+       cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking) == cudaSuccess;
+  if (!ok) {
+    ltxb_host_pipe_free(p);
+    return set_error(LTXB_ENOMEM, "host pipe: staging allocation failed");
+  }
+  *out = p;
+  return LTXB_OK;
+}
+
+int ltxb_block_forward_host(ltxb_host_pipe* p, const float* x_host, float* out_host, void* stream) {
+  if (!p || !x_host || !out_host) return set_error(LTXB_EINVAL, "null argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int b = (int)(p->calls & 1);
+  if (p->fresh) {  // the first copy of a run starts after the caller's earlier work
+    cudaEventRecord(p->start, st);
+    cudaStreamWaitEvent(p->h2d, p->start, 0);
+    p->fresh = false;
+  }
+  // x_dev[b] was last read by the compute of call k-2
+  if (p->calls >= 2) cudaStreamWaitEvent(p->h2d, p->comp_done[b], 0);
+  cudaError_t e = cudaMemcpyAsync(p->x_dev[b], x_host, p->bytes, cudaMemcpyHostToDevice, p->h2d);
+  if (e != cudaSuccess) return set_cuda_error(e, "host pipe: H2D");
+  cudaEventRecord(p->h2d_done[b], p->h2d);
+  cudaStreamWaitEvent(st, p->h2d_done[b], 0);
+  // out_dev[b] was last copied out by the D2H of call k-2
+  if (p->calls >= 2) cudaStreamWaitEvent(st, p->d2h_done[b], 0);
+  ltxb_block_io io = p->io;
+  io.x = p->x_dev[b];
+  io.out = p->out_dev[b];
+  int rc = run_block(p->w, &io, &p->cfg, LTXB_STAGE_BLOCK_OUT, nullptr, st);
+  if (rc) return rc;
+  cudaEventRecord(p->comp_done[b], st);
+  cudaStreamWaitEvent(p->d2h, p->comp_done[b], 0);
+  e = cudaMemcpyAsync(out_host, p->out_dev[b], p->bytes, cudaMemcpyDeviceToHost, p->d2h);
+  if (e != cudaSuccess) return set_cuda_error(e, "host pipe: D2H");
+  cudaEventRecord(p->d2h_done[b], p->d2h);
+  p->calls += 1;
+  return LTXB_OK;
+}
+
+int ltxb_host_pipe_join(ltxb_host_pipe* p, void* stream) {
+  if (!p) return set_error(LTXB_EINVAL, "null pipe");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < 2 && i < p->calls; ++i) {
+    cudaStreamWaitEvent(st, p->d2h_done[i], 0);
+    cudaStreamWaitEvent(st, p->h2d_done[i], 0);
+  }
+  p->fresh = true;
+  return LTXB_OK;
 }
 
 // ---- communicator ----

@@ -72,8 +72,13 @@ def _load() -> ctypes.CDLL:
         "ltxb_comm_init": (i32, [vp, i32, i32, i32, ctypes.POINTER(vp)]),
         "ltxb_comm_free": (None, [vp]),
         "ltxb_block_workspace_bytes": (u64, [vp, vp]),
+        "ltxb_ring_step": (i32, [i32, i32, i32, vp, vp, vp, vp]),
         "ltxb_block_forward": (i32, [vp, vp, vp, vp]),
         "ltxb_block_stage": (i32, [vp, vp, vp, i32, vp, vp]),
+        "ltxb_host_pipe_create": (i32, [vp, vp, vp, ctypes.POINTER(vp)]),
+        "ltxb_block_forward_host": (i32, [vp, vp, vp, vp]),
+        "ltxb_host_pipe_join": (i32, [vp, vp]),
+        "ltxb_host_pipe_free": (None, [vp]),
         "ltxb_attention": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, f32, vp]),
         "ltxb_dq_gemm": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, vp, u64, vp]),
         "ltxb_gemm_bf16": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
@@ -267,6 +272,15 @@ def build_quant_bufs(blob: Blob, block_idx: int, qset: int = QSET_REF, hidden: i
 # communicator (sequence parallelism)
 # ---------------------------------------------------------------------------
 
+def ring_step(rank: int, nranks: int, step: int) -> dict:
+    """The library's ring schedule (ltxb_ring_step): which K/V shard this rank
+    attends to at `step`, which shard it receives meanwhile (-1 on the last
+    step), and its ring neighbours."""
+    out = [ctypes.c_int() for _ in range(4)]
+    _check(lib.ltxb_ring_step(rank, nranks, step, *[ctypes.byref(o) for o in out]))
+    return dict(compute=out[0].value, recv=out[1].value, next=out[2].value, prev=out[3].value)
+
+
 class Comm:
     """NCCL communicator for the ring of K/V shards (one rank per GPU)."""
 
@@ -356,6 +370,10 @@ class Block:
                                     _stream(stream)))
         return out
 
+    def host_pipe(self, tstab, tidx, ctx, pts2, cos, sin, T: int) -> "HostPipe":
+        """A pipelined host-buffer runner bound to these device tables."""
+        return HostPipe(self, tstab, tidx, ctx, pts2, cos, sin, T)
+
     # the reference's method names (ltx/block.zig:248-353)
     def blockOut(self, x, tstab, tidx, ctx, pts2, cos, sin):
         return self.forward(x, tstab, tidx, ctx, pts2, cos, sin)
@@ -391,6 +409,45 @@ class Block:
 
     def s7FfOut(self, *a):
         return self.stage("s7_ff_out", *a)
+
+
+class HostPipe:
+    """ltxb_host_pipe: x from pinned host memory in, block output to pinned
+    host memory out, with the copies of neighbouring calls overlapping the
+    compute (see include/ltxb.h)."""
+
+    def __init__(self, blk: Block, tstab, tidx, ctx, pts2, cos, sin, T: int):
+        self.blk = blk
+        self._keep = (tstab, tidx, ctx, pts2, cos, sin)
+        S, K = ctx.shape[0], tstab.shape[0]
+        c = blk._cfg(T, S, K)
+        nbytes = lib.ltxb_block_workspace_bytes(blk.w.handle, ctypes.byref(c))
+        self._ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=ctx.device)
+        base = self._ws.data_ptr()
+        aligned = (base + 255) & ~255
+        io = _IO(None, None, _ptr(tstab), _ptr(tidx), _ptr(ctx), _ptr(pts2), _ptr(cos), _ptr(sin), aligned,
+                 self._ws.numel() - (aligned - base))
+        h = ctypes.c_void_p()
+        _check(lib.ltxb_host_pipe_create(blk.w.handle, ctypes.byref(c), ctypes.byref(io), ctypes.byref(h)))
+        self.handle = h
+
+    def forward(self, x_host: torch.Tensor, out_host: torch.Tensor, stream=None) -> None:
+        assert not x_host.is_cuda and not out_host.is_cuda and x_host.is_contiguous() and out_host.is_contiguous()
+        _check(lib.ltxb_block_forward_host(self.handle, x_host.data_ptr(), out_host.data_ptr(), _stream(stream)))
+
+    def join(self, stream=None) -> None:
+        _check(lib.ltxb_host_pipe_join(self.handle, _stream(stream)))
+
+    def free(self) -> None:
+        if self.handle:
+            lib.ltxb_host_pipe_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 class QBlock(Block):

@@ -147,3 +147,26 @@ def test_upload_errors(cuda):
     inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 0, "axes", 3, "random")
     with pytest.raises(ltxb.LtxbError):
         blk.forward(*helpers.to_cuda(inp, cuda))
+
+
+def test_host_pipe_matches_device_forward(cuda):
+    """ltxb_block_forward_host: pipelined host-buffer calls give exactly the
+    device-buffer results, call by call (double-buffered staging reused)."""
+    import ltxb
+    geom, bw, data, ent, _ = helpers.weights_case(SMALL["d"], SMALL["ff"], 2, "int8")
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 2, "axes", 3, "random")
+    w = helpers.upload(data, ent, geom, ltxb.MODE_INT8)
+    blk = ltxb.QBlock(w)
+    x, tstab, tidx, ctx, pts2, cos, sin = helpers.to_cuda(inp, cuda)
+    pipe = blk.host_pipe(tstab, tidx, ctx, pts2, cos, sin, x.shape[0])
+    xs = [(x.cpu() * (1.0 + 0.25 * i)).pin_memory() for i in range(5)]
+    outs = [torch.empty_like(xs[0]).pin_memory() for _ in xs]
+    for xi, oi in zip(xs, outs):
+        pipe.forward(xi, oi)
+    pipe.join()
+    torch.cuda.synchronize()
+    for xi, oi in zip(xs, outs):
+        want = blk.forward(xi.to(cuda), tstab, tidx, ctx, pts2, cos, sin)
+        torch.cuda.synchronize()
+        assert torch.equal(oi, want.cpu())
+    pipe.free()

@@ -1,0 +1,118 @@
+"""CPU tests of the sequence-parallel (ring attention) host logic with real
+multi-process ranks over gloo: the library's ring schedule (ltxb_ring_step,
+the same function the block's NCCL ring follows) drives a K/V shard exchange
+between world_size ranks, each rank merges per-shard (m, l, O) online-softmax
+partials, and the result must equal dense attention over all tokens."""
+
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import ltx_block_ref as ref
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _partial(q, k, v):
+    """(m, l, o) of one shard in log2 units, as the kernel's merge keeps them."""
+    c = (1.0 / math.sqrt(q.shape[-1])) * 1.4426950408889634
+    s = torch.einsum("qhd,khd->hqk", q, k) * c
+    m = s.amax(-1)
+    p = torch.exp2(s - m[..., None])
+    return m, p.sum(-1), torch.einsum("hqk,khd->hqd", p, v)
+
+
+def _ring_worker(rank, world, port, T, H, seed, result_q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "ltx-zml_b200")]
+    import ltxb
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(seed)
+        q_all = torch.randn(world * T, H, 128, generator=g, dtype=torch.float64)
+        k_all = torch.randn(world * T, H, 128, generator=g, dtype=torch.float64)
+        v_all = torch.randn(world * T, H, 128, generator=g, dtype=torch.float64)
+        sl = slice(rank * T, (rank + 1) * T)
+        q = q_all[sl]
+        shards_k = {rank: k_all[sl].clone()}
+        shards_v = {rank: v_all[sl].clone()}
+        m = l = o = None
+        for s in range(world):
+            st = ltxb.ring_step(rank, world, s)
+            cur = st["compute"]
+            reqs = []
+            if st["recv"] >= 0:
+                rk = torch.empty_like(shards_k[cur])
+                rv = torch.empty_like(shards_v[cur])
+                reqs = [dist.isend(shards_k[cur], st["next"]), dist.isend(shards_v[cur], st["next"]),
+                        dist.irecv(rk, st["prev"]), dist.irecv(rv, st["prev"])]
+            mi, li, oi = _partial(q, shards_k[cur], shards_v[cur])
+            if m is None:
+                m, l, o = mi, li, oi
+            else:
+                mn = torch.maximum(m, mi)
+                a, b = torch.exp2(m - mn), torch.exp2(mi - mn)
+                l = l * a + li * b
+                o = o * a[..., None] + oi * b[..., None]
+                m = mn
+            for r_ in reqs:
+                r_.wait()
+            if st["recv"] >= 0:
+                shards_k[st["recv"]], shards_v[st["recv"]] = rk, rv
+        out = (o / l[..., None]).permute(1, 0, 2)
+        want = ref.sdpa_dense(q, k_all, v_all)
+        seen = sorted(shards_k)
+        result_q.put((rank, ref.rel_rms(out, want), seen))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_ring_attention_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, 48, 2, 7, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, seen in res:
+        assert err < 1e-12, (rank, err)
+        assert seen == list(range(world)), "every rank must receive every shard exactly once"
+
+
+def test_ring_schedule_properties():
+    """Every rank attends to every shard exactly once; the shard received at
+    step s is the one computed at step s+1; sends form a ring."""
+    import ltxb
+    for n in (1, 2, 4, 8):
+        for r in range(n):
+            steps = [ltxb.ring_step(r, n, s) for s in range(n)]
+            assert sorted(st["compute"] for st in steps) == list(range(n))
+            assert steps[0]["compute"] == r
+            for s in range(n - 1):
+                assert steps[s]["recv"] == steps[s + 1]["compute"]
+            assert steps[-1]["recv"] == -1
+            assert steps[0]["next"] == (r + 1) % n and steps[0]["prev"] == (r - 1) % n
+            # what r receives at step s is what prev computed (and sent) at step s
+            for s in range(n - 1):
+                assert steps[s]["recv"] == ltxb.ring_step(steps[0]["prev"], n, s)["compute"]
+    with pytest.raises(ltxb.LtxbError):
+        ltxb.ring_step(2, 2, 0)
