@@ -1,0 +1,79 @@
+"""Operator micro-benchmarks of libltxb.so (one kernel family per run), for
+timing and for sizing profiler captures:
+
+    PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench attention --T 8192 --H 8 --reps 3
+    PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench dq_gemm --M 8192 --N 4096 --K 4096 [--unfused]
+    PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench gemm --M 8192 --N 4096 --K 4096
+
+Inputs are seeded N(0, 1) activations and N(0, 0.02) weights generated on the
+device; each run prints one line with the CUDA-event time per launch and the
+algorithmic throughput.
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import attention, dq_gemm, gemm_bf16, device_status
+
+
+def _time(fn, reps: int) -> float:
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op", choices=("attention", "dq_gemm", "gemm"))
+    ap.add_argument("--T", type=int, default=8192)
+    ap.add_argument("--Tkv", type=int, default=0)
+    ap.add_argument("--H", type=int, default=8)
+    ap.add_argument("--M", type=int, default=8192)
+    ap.add_argument("--N", type=int, default=4096)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--unfused", action="store_true")
+    ap.add_argument("--reps", type=int, default=10)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    if a.op == "attention":
+        tkv = a.Tkv or a.T
+        q = torch.randn(a.T, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
+        k = torch.randn(tkv, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn(tkv, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        ms = _time(lambda: attention(q, k, v, out=out), a.reps)
+        flop = 4.0 * a.T * tkv * a.H * 128
+        print(f"attention T={a.T} Tkv={tkv} H={a.H}: {ms:.4f} ms/launch {flop / ms / 1e9:.1f} TFLOP/s "
+              f"status={device_status()}")
+    else:
+        x = torch.randn(a.M, a.K, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.randn(a.N, a.K, generator=g, device=dev) * 0.02
+        out = torch.empty(a.M, a.N, dtype=torch.bfloat16, device=dev)
+        if a.op == "gemm":
+            wb = w.to(torch.bfloat16)
+            ms = _time(lambda: gemm_bf16(x, wb, out=out), a.reps)
+        else:
+            wg = w.view(a.N, a.K // 128, 128)
+            sc = (wg.abs().amax(-1, keepdim=True) / 127.0).clamp_min(1e-12).to(torch.bfloat16)
+            wq = torch.clamp(torch.round(wg / sc.float()), -128, 127).to(torch.int8).view(a.N, a.K)
+            sc = sc.view(a.N, a.K // 128).contiguous()
+            ws = None if not a.unfused else torch.empty(a.N * a.K * 2, dtype=torch.uint8, device=dev)
+            ms = _time(lambda: dq_gemm(x, wq, sc, fused=not a.unfused, out=out, workspace=ws), a.reps)
+        flop = 2.0 * a.M * a.N * a.K
+        print(f"{a.op}{' unfused' if a.unfused else ''} M={a.M} N={a.N} K={a.K}: {ms:.4f} ms/launch "
+              f"{flop / ms / 1e9:.1f} TFLOP/s status={device_status()}")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
