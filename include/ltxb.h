@@ -263,6 +263,26 @@ int ltxb_attention(const void* q, const void* k, const void* v, void* out, const
 int ltxb_dq_gemm(const void* A, const void* Wq, const void* scales, int scale_dtype, const void* bias, void* out,
                  int M, int N, int K, int fused, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* Size of the scratch ltxb_dq_gemm_noalloc keeps in the library image. */
+#define LTXB_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* The int8 grouped-128 linear of ltxb_dq_gemm (expand-then-GEMM path) for
+ * callers that cannot call cudaMalloc: hosts whose device memory belongs to
+ * another allocator (a Zig host with a fixed arena, a serving process with
+ * its own caching allocator) or code that must not allocate while it runs.
+ * No counterpart in the reference: its ZML runtime always allocates. The
+ * bf16 expansion of Wq lives in a fixed LTXB_NOALLOC_SCRATCH_BYTES array
+ * inside the library (held on every GPU that loads the library until the
+ * process exits), so N * K * 2 must not exceed it (N * K <= 16,777,216, e.g.
+ * 4096 x 4096); larger requests return LTXB_EINVAL. The caller passes A, the
+ * weights, scales, bias and out as for ltxb_dq_gemm. The first call on a
+ * device looks up the scratch address for that device; make that first call
+ * before any stream capture. All calls share the one scratch array: calls
+ * whose work overlaps on the GPU (different streams) race on it. Nothing in
+ * it needs to start at zero -- each call overwrites the part it reads. */
+int ltxb_dq_gemm_noalloc(const void* A, const void* Wq, const void* scales, int scale_dtype, const void* bias,
+                         void* out, int M, int N, int K, void* stream);
+
 /* out[M, N] (bf16) = A[M, K] (bf16) . W[N, K] (bf16)^T (+ bias): the plain
  * bf16 `lin` on tcgen05. */
 int ltxb_gemm_bf16(const void* A, const void* W, const void* bias, void* out, int M, int N, int K, void* stream);
