@@ -3,12 +3,13 @@
 // zml.nn.sdpa it agrees with (ltx/block.zig:234, gate ltx/block_conformance.zig:406).
 //
 // CTA = two 128-row query tiles (A, B) of one head sharing every K/V tile,
-// 320 threads:
-//   warps 0..3  softmax of tile A: thread i owns query row i (TMEM lane i)
-//   warps 4..7  softmax of tile B
-//   warp 8      TMA producer: Q_A, Q_B once, then K_j / V_j (128 x 128 bf16)
-//               into a 2-stage ring with separate K and V barriers
-//   warp 9      TMEM owner + single-thread tcgen05.mma issuer
+// 576 threads:
+//   warps 0..7   softmax of tile A: query row i lives in TMEM lane i and is
+//                served by two warps, one per 64-column half of the scores
+//   warps 8..15  softmax of tile B
+//   warp 16      TMA producer: Q_A, Q_B once, then K_j / V_j (128 x 128 bf16)
+//                into a 2-stage ring with separate K and V barriers
+//   warp 17      TMEM owner + single-thread tcgen05.mma issuer
 // TMEM (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
 // The softmax writes P_X (bf16 pairs) back over the first 64 columns of S_X,
 // and O_X += P_X V_j reads its A operand straight from TMEM.
@@ -22,7 +23,8 @@
 // Softmax per row: scores in log2 units, a running reference max that only
 // moves (with an O rescale in TMEM) when the tile max exceeds it by more than
 // 2^8, exp2 split between the MUFU unit and a degree-3 polynomial on the FMA
-// pipe, row sums in f32. K/V rows past Tkv are zero-filled by TMA and masked;
+// pipe (6 of 16 pairs), row sums in f32; the per-pair arithmetic uses the
+// two-wide f32 instructions (fma/add .f32x2, 3-input max). K/V rows past Tkv are zero-filled by TMA and masked;
 // query rows past Tq are computed and dropped.
 //
 // Ring attention: with MERGE, the kernel processes one K/V shard and merges
@@ -36,8 +38,9 @@ constexpr int AT_BM = 128, AT_BN = 128, AT_D = 128;
 constexpr int AT_STAGES = 2;
 constexpr int AT_TILE = AT_BM * AT_D * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-col halves)
 constexpr int AT_HALF = AT_TILE / 2;
-constexpr int AT_THREADS = 320;
-constexpr int AT_SMEM = 1024 + 2 * AT_TILE /*Q_A,Q_B*/ + 2 * AT_STAGES * AT_TILE /*K,V*/ + 256;
+constexpr int AT_THREADS = 576;  // 16 softmax warps + TMA warp + MMA warp
+constexpr int AT_SMEM = 1024 + 2 * AT_TILE /*Q_A,Q_B*/ + 2 * AT_STAGES * AT_TILE /*K,V*/ + 256 +
+                        (2 * 2 * 2 + 2 * 2) * AT_BM * 4 /*row-max (x2 buffers) and row-sum exchange*/;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when the max grows by > 2^8
 
 __device__ __forceinline__ float ex2_mufu(float x) {
@@ -64,6 +67,50 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// Two-wide f32 SIMD (sm_100 `*.f32x2`) on register pairs.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// ex2_poly for a pair, the range reduction and polynomial in f32x2.
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& p1) {
+  x0 = fmaxf(x0, -120.0f);
+  x1 = fmaxf(x1, -120.0f);
+  const uint64_t x2 = pk2(x0, x1);
+  const uint64_t t2 = add2(x2, pk2(12582912.0f, 12582912.0f));
+  const uint64_t n2 = add2(t2, pk2(-12582912.0f, -12582912.0f));
+  const uint64_t f2 = fma2(n2, pk2(-1.0f, -1.0f), x2);
+  uint64_t q2 = fma2(pk2(0.05508868396282196f, 0.05508868396282196f), f2,
+                     pk2(0.24260404706001282f, 0.24260404706001282f));
+  q2 = fma2(q2, f2, pk2(0.6932762265205383f, 0.6932762265205383f));
+  q2 = fma2(q2, f2, pk2(0.9999289512634277f, 0.9999289512634277f));
+  float t0, t1;
+  up2(q2, p0, p1);
+  up2(t2, t0, t1);
+  p0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 template <bool MERGE>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -82,6 +129,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   uint64_t* p_full = bars + 9;    // [tile]
   uint64_t* o_done = bars + 11;   // [tile]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  float* xmax = reinterpret_cast<float*>(bars + 32);  // [2 bufs][2 tiles][2 halves][128]
+  float* xsum = xmax + 2 * 2 * 2 * AT_BM;             // [2 tiles][2 halves][128]
 
   const int warp = warp_id(), lane = lane_id();
   const int q0 = blockIdx.x * (2 * AT_BM), h = blockIdx.y;
@@ -96,23 +145,23 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 8);
       mbar_init(&o_done[i], 1);
     }
     fence_mbar_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == 16 && lane == 0) {
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
   }
-  if (warp == 9) tmem_alloc(tmem_slot, 512);
+  if (warp == 17) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == 16) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, 2 * AT_TILE);
@@ -133,7 +182,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tma_load_2d(v + AT_HALF, &tmV, &v_full[st], col0 + 64, j * AT_BN);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 17) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(AT_BM, AT_BN, 0, 0);
@@ -188,122 +237,137 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
     }
   } else {
-    // ---------------- softmax / correction / epilogue (warps 0..7) ----------------
-    const int tile = warp >> 2;  // 0 = A, 1 = B
+    // ---------------- softmax / correction / epilogue (warps 0..15) ----------------
+    // Two warps per query row: warp w serves tile w / 8, TMEM lane quarter
+    // w % 4 and score columns [64 hf, 64 hf + 64) with hf = (w / 4) % 2. The
+    // pair exchanges its partial row maxima through shared memory once per
+    // iteration (named barrier 1 + 4 tile + quarter, 64 threads), so both
+    // halves move the reference max together.
+    const int tile = warp >> 3;  // 0 = A, 1 = B
+    const int hf = (warp >> 2) & 1;
     const int qw = warp & 3;
     const int r = qw * 32 + lane;
+    const uint32_t bar_id = 1 + tile * 4 + qw;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     const uint32_t tS = tmem + tile * 128 + lane_off;
-    const uint32_t tO = tmem + 256 + tile * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + tile * 128 + lane_off + hf * 64;
     const float c = args.scale * 1.4426950408889634f;  // scores -> log2 units
-    float m_ref = -INFINITY, l = 0.f;  // m_ref in log2 units
+    float m_ref = -INFINITY, l = 0.f;  // m_ref in log2 units, l over this warp's columns
     bool ok = true;
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
+    // Every warp of a pair passes the same pair barriers (one per iteration,
+    // one in the epilogue) even after a timed-out wait, so that a failure in
+    // one warp can never leave its partner blocked on the named barrier.
     for (int j = 0; j < nkv; ++j) {
-      if (!warp_wait(&s_full[tile], j & 1, 0x208)) { ok = false; break; }
+      if (ok && !warp_wait(&s_full[tile], j & 1, 0x208)) ok = false;
+      float* xm = xmax + (((j & 1) * 2 + tile) * 2) * AT_BM;
+      if (!ok) {
+        xm[hf * AT_BM + r] = -INFINITY;
+        pair_sync();
+        continue;
+      }
       tc_fence_after();
-      // One streaming pass over the 128 scores in four 32-column chunks (the
-      // next chunk's TMEM load overlaps this chunk's math). p = 2^(s c - m)
-      // uses the running reference max m; a chunk whose max exceeds m by more
-      // than 2^8 moves m up and rescales what this row already holds (l, the
-      // P chunks written this iteration, and O from earlier iterations).
-      // P chunk k (bf16 pairs) goes to columns [16k, 16k + 16), all of which
-      // were read before.
-      const int valid = Tkv - j * AT_BN;  // columns < valid are real keys
-      float sum = 0.f;
-      uint32_t cur[32], nxt[32];
-      tmem_ld32(tS, cur);
+      uint32_t c0[32], c1[32];
+      tmem_ld32(tS + hf * 64, c0);
+      tmem_ld32(tS + hf * 64 + 32, c1);
       tmem_wait_ld();
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        if (ch < 3) tmem_ld32(tS + (ch + 1) * 32, nxt);
-        float v[32];  // raw scores; c > 0 so max(v) * c is the max in log2 units
+      const int valid = Tkv - j * AT_BN - hf * 64;  // this warp's columns < valid are real keys
+      if (valid < 64) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(cur[e]);
-        if (valid < AT_BN) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (ch * 32 + e >= valid) v[e] = -INFINITY;
-        }
-        float m4[4] = {v[0], v[1], v[2], v[3]};
-#pragma unroll
-        for (int e = 4; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], v[e]);
-        const float cm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * c;
-        const bool need = cm > m_ref + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, need)) {
-          const float m_new = need ? cm : m_ref;
-          const float corr = ex2_mufu(m_ref - m_new);  // 0 on the very first chunk
-          m_ref = m_new;
-          l *= corr;
-          sum *= corr;
-          if (ch > 0) {  // P chunks already written this iteration
-            tmem_wait_st();
-            uint32_t pp[32];
-            tmem_ld32(tS, pp);  // columns [0, 32) hold P chunks 0 and 1
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (e < 16 * ch) pp[e] = pack_bf16x2(bf16_lo(pp[e]) * corr, bf16_hi(pp[e]) * corr);
-            tmem_st32(tS, pp);
-            if (ch > 2) {
-              uint32_t p3[16];
-              // chunk 2's P lives in [32, 48): reload, scale, store
-              uint32_t q32[32];
-              tmem_ld32(tS + 32, q32);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 16; ++e) p3[e] = pack_bf16x2(bf16_lo(q32[e]) * corr, bf16_hi(q32[e]) * corr);
-              tmem_st16(tS + 32, p3);
-            }
-          }
-          if (j > 0) {  // O from earlier iterations (complete: S(j) committed after PV(j-1))
-#pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
-              uint32_t u[32];
-              tmem_ld32(tO + cc * 32, u);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
-              tmem_st32(tO + cc * 32, u);
-            }
-          }
-        }
-        const float mc = m_ref;
-        uint32_t pk[16];
-        float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          // 3 of every 8 exponentials on the FMA pipe, the rest on MUFU
-          const float a0 = fmaf(v[2 * e], c, -mc), a1 = fmaf(v[2 * e + 1], c, -mc);
-          const float p0 = ((e & 3) == 1) ? ex2_poly(a0) : ex2_mufu(a0);
-          const float p1 = ((e & 1) == 1) ? ex2_poly(a1) : ex2_mufu(a1);
-          s4[e & 3] += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
-        }
-        sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
-        tmem_st16(tS + ch * 16, pk);
-        if (ch < 3) {
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) cur[e] = nxt[e];
+        for (int e = 0; e < 32; ++e) {
+          if (e >= valid) c0[e] = __float_as_uint(-INFINITY);
+          if (32 + e >= valid) c1[e] = __float_as_uint(-INFINITY);
         }
       }
-      l += sum;
+      float m4[4] = {__uint_as_float(c0[0]), __uint_as_float(c0[1]), __uint_as_float(c1[0]), __uint_as_float(c1[1])};
+#pragma unroll
+      for (int e = 1; e < 16; ++e) {
+        m4[(2 * e) & 3] = max3(m4[(2 * e) & 3], __uint_as_float(c0[2 * e]), __uint_as_float(c0[2 * e + 1]));
+        m4[(2 * e + 1) & 3] = max3(m4[(2 * e + 1) & 3], __uint_as_float(c1[2 * e]), __uint_as_float(c1[2 * e + 1]));
+      }
+      const float pm = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+      xm[hf * AT_BM + r] = pm;
+      pair_sync();  // both halves' S loads are complete and their maxima published
+      const float cm = fmaxf(pm, xm[(hf ^ 1) * AT_BM + r]) * c;
+      const bool need = cm > m_ref + kRescaleThreshold;
+      float corr = 1.f;
+      const bool any_need = __any_sync(0xffffffffu, need);  // same rows in both warps: same branch
+      if (any_need) {
+        const float m_new = need ? cm : m_ref;
+        corr = ex2_mufu(m_ref - m_new);  // 0 on the first iteration
+        m_ref = m_new;
+        l *= corr;
+      }
+      // p = 2^(s c - m) -> bf16 pairs over S columns [32 hf, 32 hf + 32)
+      // (keys 64 hf .. 64 hf + 63); both halves' loads finished before pair_sync
+      const uint64_t c2 = pk2(c, c), nm2 = pk2(-m_ref, -m_ref);
+      uint64_t acc2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        const uint32_t* cv = ch == 0 ? c0 : c1;
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float a0, a1, p0, p1;
+          up2(fma2(pk2(__uint_as_float(cv[2 * e]), __uint_as_float(cv[2 * e + 1])), c2, nm2), a0, a1);
+          // 6 of every 16 pairs on the FMA pipe (packed polynomial), the rest on MUFU
+          if ((e & 7) == 1 || (e & 7) == 3 || (e & 7) == 6) {
+            ex2_poly2(a0, a1, p0, p1);
+          } else {
+            p0 = ex2_mufu(a0);
+            p1 = ex2_mufu(a1);
+          }
+          acc2[e & 1] = add2(acc2[e & 1], pk2(p0, p1));
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tS + hf * 32 + ch * 16, pk);
+      }
+      {
+        float s0, s1, s2, s3;
+        up2(acc2[0], s0, s1);
+        up2(acc2[1], s2, s3);
+        l += (s0 + s1) + (s2 + s3);
+      }
+      if (any_need && j > 0) {  // this warp's half of O (complete: S(j) committed after PV(j-1))
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t u[32];
+          tmem_ld32(tO + cc * 32, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
+          tmem_st32(tO + cc * 32, u);
+        }
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[tile]);
     }
-    // ---------------- epilogue ----------------
-    if (ok && warp_wait(&o_done[tile], 0, 0x209)) {
+    // ---------------- epilogue: this warp's 64 output columns ----------------
+    const bool eok = ok && warp_wait(&o_done[tile], 0, 0x209);
+    const int row = q0 + tile * AT_BM + r;
+    const bool row_ok = row < Tq;
+    // ring merge: both halves read the old (m, l) state before the pair
+    // barrier, half 0 writes the new one after it
+    float ms = 0.f, ls = 0.f;
+    const size_t si = (size_t)h * Tq + row;
+    if (MERGE && eok && row_ok && !args.first) {
+      ms = args.m_state[si];
+      ls = args.l_state[si];
+    }
+    float* xs = xsum + tile * 2 * AT_BM;
+    xs[hf * AT_BM + r] = l;
+    pair_sync();
+    if (eok) {
       tc_fence_after();
-      const int row = q0 + tile * AT_BM + r;
-      const bool row_ok = row < Tq;
-      const size_t obase = ((size_t)row * H + h) * AT_D;
+      const float lt = l + xs[(hf ^ 1) * AT_BM + r];  // full row sum
+      const size_t obase = ((size_t)row * H + h) * AT_D + hf * 64;
       if (!MERGE) {
         const float g = (row_ok && args.gate) ? args.gate[(size_t)row * args.ldg + h] : 1.0f;
-        const float inv = g / l;
+        const float inv = g / lt;
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {
           uint32_t u[32];
           tmem_ld32(tO + cc * 32, u);
           tmem_wait_ld();
@@ -318,24 +382,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           }
         }
       } else {
-        // merge (m_ref, l, O) into the running state (m, l in log2 units)
+        // merge (m_ref, lt, O) into the running state (m, l in log2 units)
         float a = 0.f, b = 1.f;
-        const size_t si = (size_t)h * Tq + row;
         if (row_ok) {
           if (args.first) {
-            args.m_state[si] = m_ref;
-            args.l_state[si] = l;
+            if (hf == 0) {
+              args.m_state[si] = m_ref;
+              args.l_state[si] = lt;
+            }
           } else {
-            const float ms = args.m_state[si], ls = args.l_state[si];
             const float mn = fmaxf(ms, m_ref);
             a = ex2_mufu(ms - mn);
             b = ex2_mufu(m_ref - mn);
-            args.m_state[si] = mn;
-            args.l_state[si] = ls * a + l * b;
+            if (hf == 0) {
+              args.m_state[si] = mn;
+              args.l_state[si] = ls * a + lt * b;
+            }
           }
         }
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {
           uint32_t u[32];
           tmem_ld32(tO + cc * 32, u);
           tmem_wait_ld();
@@ -362,7 +428,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 done:
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 17) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
