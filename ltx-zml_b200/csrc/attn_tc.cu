@@ -9,7 +9,7 @@
 //   warps 8..15  softmax of tile B
 //   warp 16      TMA producer: Q_A, Q_B once, then K_j / V_j (128 x 128 bf16)
 //                into a 2-stage ring with separate K and V barriers
-//   warp 17      TMEM owner + single-thread tcgen05.mma issuer
+//   warp 17      TMEM owner + tcgen05.mma issuer (one elected lane)
 // TMEM (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
 // The softmax writes P_X (bf16 pairs) back over the first 64 columns of S_X,
 // and O_X += P_X V_j reads its A operand straight from TMEM.
@@ -23,12 +23,13 @@
 // Softmax per row: scores in log2 units, a running reference max that only
 // moves (with an O rescale in TMEM) when the tile max exceeds it by more than
 // 2^8, exp2 split between the MUFU unit and a degree-3 polynomial on the FMA
-// pipe (6 of 16 pairs), row sums in f32; the per-pair arithmetic uses the
+// pipe (1 of 4 pairs), row sums in f32; the per-pair arithmetic uses the
 // two-wide f32 instructions (fma/add .f32x2, 3-input max). K/V rows past Tkv are zero-filled by TMA and masked;
 // query rows past Tq are computed and dropped.
 //
 // Ring attention: with MERGE, the kernel processes one K/V shard and merges
 // its (m, l, O) into an f32 running state instead of writing the output.
+#define LTXB_LOCAL_STATUS 1  // whole-program device code (no -rdc): own status word
 #include "common.cuh"
 #include "kernels.h"
 
@@ -124,11 +125,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [2]
   uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [tile]
-  uint64_t* p_full = bars + 9;    // [tile]
-  uint64_t* o_done = bars + 11;   // [tile]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* k_empty = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [tile]
+  uint64_t* p_full = bars + 11;   // [tile]
+  uint64_t* o_done = bars + 13;   // [tile]
+  uint64_t* p_half = bars + 15;   // [tile]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   float* xmax = reinterpret_cast<float*>(bars + 32);  // [2 bufs][2 tiles][2 halves][128]
   float* xsum = xmax + 2 * 2 * 2 * AT_BM;             // [2 tiles][2 halves][128]
 
@@ -136,6 +139,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const int q0 = blockIdx.x * (2 * AT_BM), h = blockIdx.y;
   const int H = args.H, Tq = args.Tq, Tkv = args.Tkv;
   const int nkv = (Tkv + AT_BN - 1) / AT_BN;
+  // Each CTA walks the K/V tiles starting from its own offset (step i reads
+  // tile (i + kv0) mod nkv): the CTAs resident at one time then stream
+  // different tiles instead of all requesting the same lines of L2 at once.
+  // Online softmax is order-independent; the order is fixed per CTA, so
+  // results stay deterministic.
+  const int kv0 = (int)(((long long)blockIdx.x * nkv) / gridDim.x);
+  auto kv_tile = [&](int i) { const int t = i + kv0; return t >= nkv ? t - nkv : t; };
   const int col0 = h * AT_D;
 
   if (threadIdx.x == 0) {
@@ -143,9 +153,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 8);
+      mbar_init(&p_half[i], 8);
       mbar_init(&o_done[i], 1);
     }
     fence_mbar_init();
@@ -160,83 +172,118 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  // Warps 16 and 17 run their loops with all 32 lanes (warp-uniform control
+  // flow and operands, so descriptors and addresses stay in uniform
+  // registers) and let one elected lane issue each copy / MMA / commit.
   if (warp == 16) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
+    if (elect_one()) {
       mbar_arrive_expect_tx(q_full, 2 * AT_TILE);
       tma_load_2d(sQ, &tmQ, q_full, col0, q0);
       tma_load_2d(sQ + AT_HALF, &tmQ, q_full, col0 + 64, q0);
       tma_load_2d(sQ + AT_TILE, &tmQ, q_full, col0, q0 + AT_BM);
       tma_load_2d(sQ + AT_TILE + AT_HALF, &tmQ, q_full, col0 + 64, q0 + AT_BM);
-      for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, 0x201)) goto done;
-        uint8_t* k = sK + st * AT_TILE;
-        uint8_t* v = sV + st * AT_TILE;
+    }
+    __syncwarp();
+    for (int j = 0; j < nkv; ++j) {
+      // K_j and V_j have separate free signals: K's stage frees once both
+      // S MMAs of step j-2 are done, V's once both PV MMAs are, so each
+      // load starts about one and a half steps before its first use.
+      const int st = j & 1;
+      uint8_t* k = sK + st * AT_TILE;
+      uint8_t* v = sV + st * AT_TILE;
+      const int krow = kv_tile(j) * AT_BN;
+      if (!warp_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, 0x201)) goto done;
+      if (elect_one()) {
         mbar_arrive_expect_tx(&k_full[st], AT_TILE);
-        tma_load_2d(k, &tmK, &k_full[st], col0, j * AT_BN);
-        tma_load_2d(k + AT_HALF, &tmK, &k_full[st], col0 + 64, j * AT_BN);
-        mbar_arrive_expect_tx(&v_full[st], AT_TILE);
-        tma_load_2d(v, &tmV, &v_full[st], col0, j * AT_BN);
-        tma_load_2d(v + AT_HALF, &tmV, &v_full[st], col0 + 64, j * AT_BN);
+        tma_load_2d(k, &tmK, &k_full[st], col0, krow);
+        tma_load_2d(k + AT_HALF, &tmK, &k_full[st], col0 + 64, krow);
       }
+      __syncwarp();
+      if (!warp_wait(&v_empty[st], ((j >> 1) & 1) ^ 1, 0x20a)) goto done;
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&v_full[st], AT_TILE);
+        tma_load_2d(v, &tmV, &v_full[st], col0, krow);
+        tma_load_2d(v + AT_HALF, &tmV, &v_full[st], col0 + 64, krow);
+      }
+      __syncwarp();
     }
   } else if (warp == 17) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(AT_BM, AT_BN, 0, 0);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(AT_BM, AT_D, 0, 1);
-      const uint32_t qa = smem_u32(sQ);
-      auto issue_s = [&](int tile, int j) {
-        const uint32_t ka = smem_u32(sK + (j & 1) * AT_TILE);
-        const uint32_t qt = qa + tile * AT_TILE;
+    constexpr uint32_t idesc_s = idesc_bf16_f32(AT_BM, AT_BN, 0, 0);
+    constexpr uint32_t idesc_o = idesc_bf16_f32(AT_BM, AT_D, 0, 1);
+    const uint32_t qa = smem_u32(sQ);
+    auto issue_s = [&](int tile, int j) {
+      const uint32_t ka = smem_u32(sK + (j & 1) * AT_TILE);
+      const uint32_t qt = qa + tile * AT_TILE;
+      if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * AT_HALF + (kk & 3) * 32;
           umma_ss(tmem + tile * 128, sdesc_kmajor_sw128(qt + off), sdesc_kmajor_sw128(ka + off), idesc_s, kk > 0);
         }
         umma_commit(&s_full[tile]);
-      };
-      auto issue_pv = [&](int tile, int j) {
-        const uint32_t va = smem_u32(sV + (j & 1) * AT_TILE);
+      }
+      __syncwarp();
+    };
+    // PV in two halves of the K (key) steps: part 0 = steps 0, 1, 4, 5 (the
+    // P chunks the softmax warps hand over first), part 1 = steps 2, 3, 6, 7.
+    auto issue_pv = [&](int tile, int j, int part) {
+      const uint32_t va = smem_u32(sV + (j & 1) * AT_TILE);
+      if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int i = 0; i < 4; ++i) {
+          const int kk = (i & 1) + (i >> 1) * 4 + part * 2;
           umma_ts(tmem + 256 + tile * 128, tmem + tile * 128 + kk * 8, sdesc_mnmajor_sw128(va + kk * 2048, AT_HALF),
-                  idesc_o, (j | kk) != 0);
-      };
-      if (!mbar_wait(q_full, 0, 0x202)) goto done;
-      if (!mbar_wait(&k_full[0], 0, 0x203)) goto done;
-      tc_fence_after();
-      issue_s(0, 0);
-      issue_s(1, 0);
-      for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        const bool more = j + 1 < nkv;
-        // tile A: O_A += P_A V_j, then S_A(j+1)
-        if (!mbar_wait(&p_full[0], j & 1, 0x204)) goto done;
-        if (!mbar_wait(&v_full[st], (j >> 1) & 1, 0x205)) goto done;
-        tc_fence_after();
-        issue_pv(0, j);
-        if (more) {
-          if (!mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1, 0x206)) goto done;
-          tc_fence_after();
-          issue_s(0, j + 1);
-        } else {
-          umma_commit(&o_done[0]);
+                  idesc_o, (j | part | i) != 0);
         }
-        // tile B
-        if (!mbar_wait(&p_full[1], j & 1, 0x207)) goto done;
+      }
+      __syncwarp();
+    };
+    auto commit = [&](uint64_t* bar) {
+      if (elect_one()) umma_commit(bar);
+      __syncwarp();
+    };
+    if (!warp_wait(q_full, 0, 0x202)) goto done;
+    if (!warp_wait(&k_full[0], 0, 0x203)) goto done;
+    tc_fence_after();
+    issue_s(0, 0);
+    issue_s(1, 0);
+    commit(&k_empty[0]);  // K_0 consumed by both S MMAs
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      const bool more = j + 1 < nkv;
+      // tile A: O_A += P_A V_j, then S_A(j+1)
+      if (!warp_wait(&v_full[st], (j >> 1) & 1, 0x205)) goto done;  // normally long ready
+      if (!warp_wait(&p_half[0], j & 1, 0x20b)) goto done;
+      tc_fence_after();
+      issue_pv(0, j, 0);
+      if (!warp_wait(&p_full[0], j & 1, 0x204)) goto done;
+      tc_fence_after();
+      issue_pv(0, j, 1);
+      if (more) {
+        if (!warp_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1, 0x206)) goto done;
         tc_fence_after();
-        issue_pv(1, j);
-        umma_commit(&kv_empty[st]);  // K_j, V_j consumed by every MMA issued so far
-        if (more)
-          issue_s(1, j + 1);
-        else
-          umma_commit(&o_done[1]);
+        issue_s(0, j + 1);
+      } else {
+        commit(&o_done[0]);
+      }
+      // tile B
+      if (!warp_wait(&p_half[1], j & 1, 0x20c)) goto done;
+      tc_fence_after();
+      issue_pv(1, j, 0);
+      if (!warp_wait(&p_full[1], j & 1, 0x207)) goto done;
+      tc_fence_after();
+      issue_pv(1, j, 1);
+      commit(&v_empty[st]);  // V_j consumed by both PV MMAs
+      if (more) {
+        issue_s(1, j + 1);
+        commit(&k_empty[st ^ 1]);  // K_{j+1} consumed by both S MMAs
+      } else {
+        commit(&o_done[1]);
       }
     }
-  } else {
+  } else if (warp < 16) {
     // ---------------- softmax / correction / epilogue (warps 0..15) ----------------
     // Two warps per query row: warp w serves tile w / 8, TMEM lane quarter
     // w % 4 and score columns [64 hf, 64 hf + 64) with hf = (w / 4) % 2. The
@@ -271,7 +318,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       tmem_ld32(tS + hf * 64, c0);
       tmem_ld32(tS + hf * 64 + 32, c1);
       tmem_wait_ld();
-      const int valid = Tkv - j * AT_BN - hf * 64;  // this warp's columns < valid are real keys
+      const int valid = Tkv - kv_tile(j) * AT_BN - hf * 64;  // this warp's columns < valid are real keys
       if (valid < 64) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
@@ -297,9 +344,23 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         corr = ex2_mufu(m_ref - m_new);  // 0 on the first iteration
         m_ref = m_new;
         l *= corr;
+        if (j > 0) {  // this warp's half of O (complete: S(j) committed after PV(j-1))
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t u[16];
+            tmem_ld16(tO + cc * 16, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
+            tmem_st16(tO + cc * 16, u);
+          }
+        }
       }
       // p = 2^(s c - m) -> bf16 pairs over S columns [32 hf, 32 hf + 32)
-      // (keys 64 hf .. 64 hf + 63); both halves' loads finished before pair_sync
+      // (keys 64 hf .. 64 hf + 63); both halves' loads finished before
+      // pair_sync. Chunk 0 (keys 64 hf .. 64 hf + 31) is handed to the MMA
+      // warp on its own (p_half), so the PV K-steps over keys 0-31 and 64-95
+      // run while chunk 1 is computed.
       const uint64_t c2 = pk2(c, c), nm2 = pk2(-m_ref, -m_ref);
       uint64_t acc2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
 #pragma unroll
@@ -310,8 +371,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         for (int e = 0; e < 16; ++e) {
           float a0, a1, p0, p1;
           up2(fma2(pk2(__uint_as_float(cv[2 * e]), __uint_as_float(cv[2 * e + 1])), c2, nm2), a0, a1);
-          // 6 of every 16 pairs on the FMA pipe (packed polynomial), the rest on MUFU
-          if ((e & 7) == 1 || (e & 7) == 3 || (e & 7) == 6) {
+          // 1 of every 4 pairs on the FMA pipe (packed polynomial), the rest on MUFU
+          if ((e & 3) == 1) {
             ex2_poly2(a0, a1, p0, p1);
           } else {
             p0 = ex2_mufu(a0);
@@ -321,6 +382,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           pk[e] = pack_bf16x2(p0, p1);
         }
         tmem_st16(tS + hf * 32 + ch * 16, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ch == 0 ? &p_half[tile] : &p_full[tile]);
       }
       {
         float s0, s1, s2, s3;
@@ -328,21 +393,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         up2(acc2[1], s2, s3);
         l += (s0 + s1) + (s2 + s3);
       }
-      if (any_need && j > 0) {  // this warp's half of O (complete: S(j) committed after PV(j-1))
-#pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-          uint32_t u[32];
-          tmem_ld32(tO + cc * 32, u);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
-          tmem_st32(tO + cc * 32, u);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[tile]);
     }
     // ---------------- epilogue: this warp's 64 output columns ----------------
     const bool eok = ok && warp_wait(&o_done[tile], 0, 0x209);
@@ -484,6 +534,15 @@ int attention_tc(const AttnArgs& a, cudaStream_t st) {
     return set_error(LTXB_EINVAL, "attention: q/k/v/out must be 16-byte aligned");
   if (a.o_acc) return launch_attn<true>(a, st);
   return launch_attn<false>(a, st);
+}
+
+cudaError_t attn_status(uint32_t* v, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(v, g_status, sizeof(*v));
+  if (e == cudaSuccess && clear && *v) {
+    const uint32_t z = 0;
+    e = cudaMemcpyToSymbol(g_status, &z, sizeof(z));
+  }
+  return e;
 }
 
 int attention_finalize(const AttnArgs& a, cudaStream_t st) {

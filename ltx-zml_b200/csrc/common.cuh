@@ -22,7 +22,15 @@ namespace ltxb {
 // bits 0..7: status code, bits 8..31: site of the first failure.
 enum : uint32_t { STATUS_OK = 0, STATUS_TIMEOUT = 1 };
 
+#ifdef LTXB_LOCAL_STATUS
+// A translation unit built as whole-program device code (no -rdc: ptxas then
+// sees the whole kernel, and honours setmaxnreg) keeps its own status word;
+// the host reads it through that unit's accessor and merges it with the
+// shared one.
+static __device__ uint32_t g_status = 0;
+#else
 extern __device__ uint32_t g_status;
+#endif
 
 __device__ __forceinline__ void report_timeout(uint32_t site) {
   atomicCAS(&g_status, 0u, STATUS_TIMEOUT | (site << 8));
@@ -91,6 +99,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
       }
     }
   }
+}
+
+// One lane of a fully active warp (elect.sync): warp-uniform roles issue their
+// asynchronous copies / MMAs / commits from it.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, px;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // Warp-uniform wait for roles whose lanes run .sync.aligned instructions

@@ -95,6 +95,8 @@ struct AttnArgs {
 };
 int attention_tc(const AttnArgs& a, cudaStream_t st);
 int attention_finalize(const AttnArgs& a, cudaStream_t st);
+// status word of the attention unit (compiled separately, see common.cuh)
+cudaError_t attn_status(uint32_t* v, bool clear);
 
 // ---- elementwise / normalisation kernels ----
 // n = rms(x) * (1 + ada(r_scale)) + ada(r_shift) -> bf16 or f32 [T, D]

@@ -213,6 +213,10 @@ int ltxb_device_status(int clear, uint32_t* site) {
     e = cudaMemcpyToSymbol(g_status, &z, sizeof(z));
     if (e != cudaSuccess) return set_cuda_error(e, "clear status");
   }
+  uint32_t va = 0;
+  e = ltxb::attn_status(&va, clear != 0);
+  if (e != cudaSuccess) return set_cuda_error(e, "read attention status");
+  if (!v) v = va;
   if (site) *site = v >> 8;
   if ((v & 0xFF) == STATUS_TIMEOUT) return set_error(LTXB_ETIMEOUT, "device wait expired at site 0x%x", v >> 8);
   return LTXB_OK;
