@@ -334,39 +334,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
       const float pm = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
       xm[hf * AT_BM + r] = pm;
-      pair_sync();  // both halves' S loads are complete and their maxima published
-      const float cm = fmaxf(pm, xm[(hf ^ 1) * AT_BM + r]) * c;
-      const bool need = cm > m_ref + kRescaleThreshold;
-      float corr = 1.f;
-      const bool any_need = __any_sync(0xffffffffu, need);  // same rows in both warps: same branch
-      if (any_need) {
-        const float m_new = need ? cm : m_ref;
-        corr = ex2_mufu(m_ref - m_new);  // 0 on the first iteration
-        m_ref = m_new;
-        l *= corr;
-        if (j > 0) {  // this warp's half of O (complete: S(j) committed after PV(j-1))
-#pragma unroll 1
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t u[16];
-            tmem_ld16(tO + cc * 16, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
-            tmem_st16(tO + cc * 16, u);
-          }
-        }
-      }
       // p = 2^(s c - m) -> bf16 pairs over S columns [32 hf, 32 hf + 32)
-      // (keys 64 hf .. 64 hf + 63); both halves' loads finished before
-      // pair_sync. Chunk 0 (keys 64 hf .. 64 hf + 31) is handed to the MMA
-      // warp on its own (p_half), so the PV K-steps over keys 0-31 and 64-95
-      // run while chunk 1 is computed.
-      const uint64_t c2 = pk2(c, c), nm2 = pk2(-m_ref, -m_ref);
-      uint64_t acc2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
-#pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        const uint32_t* cv = ch == 0 ? c0 : c1;
-        uint32_t pk[16];
+      // (keys 64 hf .. 64 hf + 63). Chunk 0 (keys 64 hf .. 64 hf + 31) is
+      // computed speculatively with the current reference max while the
+      // pair's max exchange completes; only when the exchange asks for a
+      // rescale (rare: the max grew by more than 2^8) is it recomputed. It is
+      // handed to the MMA warp on its own (p_half), so the PV K-steps over
+      // keys 0-31 and 64-95 run while chunk 1 is computed.
+      const uint64_t c2 = pk2(c, c);
+      uint64_t acc2[2];
+      uint32_t pk[16];
+      auto exp_chunk = [&](const uint32_t* cv) {
+        const uint64_t nm2 = pk2(-m_ref, -m_ref);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           float a0, a1, p0, p1;
@@ -381,12 +360,52 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           acc2[e & 1] = add2(acc2[e & 1], pk2(p0, p1));
           pk[e] = pack_bf16x2(p0, p1);
         }
+      };
+      auto hand_over = [&](int ch) {
         tmem_st16(tS + hf * 32 + ch * 16, pk);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(ch == 0 ? &p_half[tile] : &p_full[tile]);
+      };
+      acc2[0] = acc2[1] = pk2(0.f, 0.f);
+      exp_chunk(c0);  // speculative (at j = 0 always redone: m_ref is -inf)
+      pair_sync();    // both halves' S loads are complete and their maxima published
+      const float cm = fmaxf(pm, xm[(hf ^ 1) * AT_BM + r]) * c;
+      const bool need = cm > m_ref + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {  // same rows in both warps: same branch
+        const float m_new = need ? cm : m_ref;
+        const float corr = ex2_mufu(m_ref - m_new);  // 0 on the first iteration
+        m_ref = m_new;
+        l *= corr;
+        if (j > 0) {  // this warp's half of O (complete: S(j) committed after PV(j-1))
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t u[16];
+            tmem_ld16(tO + cc * 16, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
+            tmem_st16(tO + cc * 16, u);
+          }
+        }
+        // redo chunk 0 from S, still intact in TMEM: no P of this pair is
+        // stored before the exchange, and the partner's P never covers these
+        // columns
+        uint32_t r0[32];
+        tmem_ld32(tS + hf * 64, r0);
+        tmem_wait_ld();
+        if (valid < 32) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e >= valid) r0[e] = __float_as_uint(-INFINITY);
+        }
+        acc2[0] = acc2[1] = pk2(0.f, 0.f);
+        exp_chunk(r0);
       }
+      hand_over(0);
+      exp_chunk(c1);
+      hand_over(1);
       {
         float s0, s1, s2, s3;
         up2(acc2[0], s0, s1);
