@@ -93,6 +93,33 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
+// MMA issue with the shared-memory descriptors passed as their low words: the
+// high word of every 128-byte-swizzle descriptor here is the same constant
+// (SBO 1024 B, descriptor version 1, layout SWIZZLE_128B), and the low word
+// (start address >> 4, LBO) is stepped by plain 32-bit adds.
+constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr, uint32_t lbo_field) {
+  return ((saddr >> 4) & 0x3FFFu) | (lbo_field << 16);
+}
+__device__ __forceinline__ void mma_ss_lo(uint32_t d, uint32_t alo, uint32_t blo, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .b64 da, db;\n\t.reg .pred p;\n\t"
+      "mov.b64 da, {%1, %5};\n\tmov.b64 db, {%2, %5};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}" ::"r"(d),
+      "r"(alo), "r"(blo), "r"(idesc), "r"(acc), "r"(kDescHi)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_lo(uint32_t d, uint32_t a_tmem, uint32_t blo, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .b64 db;\n\t.reg .pred p;\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "r"(blo), "r"(idesc), "r"(acc), "r"(kDescHi)
+      : "memory");
+}
+
 // ex2_poly for a pair, the range reduction and polynomial in f32x2.
 __device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& p1) {
   x0 = fmaxf(x0, -120.0f);
@@ -214,13 +241,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     constexpr uint32_t idesc_o = idesc_bf16_f32(AT_BM, AT_D, 0, 1);
     const uint32_t qa = smem_u32(sQ);
     auto issue_s = [&](int tile, int j) {
-      const uint32_t ka = smem_u32(sK + (j & 1) * AT_TILE);
-      const uint32_t qt = qa + tile * AT_TILE;
+      const uint32_t klo = desc_lo(smem_u32(sK + (j & 1) * AT_TILE), 1);
+      const uint32_t qlo = desc_lo(qa + tile * AT_TILE, 1);
+      const uint32_t d = tmem + tile * 128;
       if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * AT_HALF + (kk & 3) * 32;
-          umma_ss(tmem + tile * 128, sdesc_kmajor_sw128(qt + off), sdesc_kmajor_sw128(ka + off), idesc_s, kk > 0);
+          const uint32_t off = ((kk >> 2) * AT_HALF + (kk & 3) * 32) >> 4;
+          mma_ss_lo(d, qlo + off, klo + off, idesc_s, kk > 0);
         }
         umma_commit(&s_full[tile]);
       }
@@ -229,13 +257,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     // PV in two halves of the K (key) steps: part 0 = steps 0, 1, 4, 5 (the
     // P chunks the softmax warps hand over first), part 1 = steps 2, 3, 6, 7.
     auto issue_pv = [&](int tile, int j, int part) {
-      const uint32_t va = smem_u32(sV + (j & 1) * AT_TILE);
+      const uint32_t vlo = desc_lo(smem_u32(sV + (j & 1) * AT_TILE), AT_HALF >> 4);
+      const uint32_t d = tmem + 256 + tile * 128, pa = tmem + tile * 128;
       if (elect_one()) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int kk = (i & 1) + (i >> 1) * 4 + part * 2;
-          umma_ts(tmem + 256 + tile * 128, tmem + tile * 128 + kk * 8, sdesc_mnmajor_sw128(va + kk * 2048, AT_HALF),
-                  idesc_o, (j | part | i) != 0);
+          mma_ts_lo(d, pa + kk * 8, vlo + kk * (2048 >> 4), idesc_o, (j | part | i) != 0);
         }
       }
       __syncwarp();
