@@ -254,6 +254,19 @@ void ltxb_host_pipe_free(ltxb_host_pipe* p);
 int ltxb_attention(const void* q, const void* k, const void* v, void* out, const float* gate, int Tq, int Tkv,
                    int H, float scale, void* stream);
 
+/* Split-K/V form of ltxb_attention for short query sequences (a
+ * sequence-parallel rank's shard against the whole sequence): the K/V tiles
+ * are divided into `splits` ranges (0 = the count that best fills the GPU),
+ * each computed into its own f32 partial state (m, l, O) in `workspace`,
+ * then merged into `out`, so that the grid covers the SMs evenly. The merge
+ * is the online-softmax combine of the reference's whileSdpa carries
+ * (ltx/block.zig:105-154). Same arguments and results as ltxb_attention
+ * otherwise; `workspace` (256-byte aligned) holds
+ * ltxb_attention_split_workspace_bytes(Tq, Tkv, H, splits) bytes. */
+uint64_t ltxb_attention_split_workspace_bytes(int Tq, int Tkv, int H, int splits);
+int ltxb_attention_split(const void* q, const void* k, const void* v, void* out, const float* gate, int Tq, int Tkv,
+                         int H, float scale, int splits, void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* out[M, N] (bf16) = A[M, K] (bf16) . dequant(Wq[N, K] int8, scales[N, K/128])^T
  * (+ bias[N] bf16, optional): the int8 grouped-128 dequant linear `linQ`
  * (ltx/block.zig:462-477). scale_dtype LTXB_DT_F32 or LTXB_DT_BF16.

@@ -165,14 +165,19 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const int warp = warp_id(), lane = lane_id();
   const int q0 = blockIdx.x * (2 * AT_BM), h = blockIdx.y;
   const int H = args.H, Tq = args.Tq, Tkv = args.Tkv;
-  const int nkv = (Tkv + AT_BN - 1) / AT_BN;
+  // this CTA's K/V tiles: [t0, t0 + nkv) of the nkv_all tiles (one split of
+  // kv_splits; the whole range without splitting)
+  const int nkv_all = (Tkv + AT_BN - 1) / AT_BN;
+  const int nsplit = MERGE && args.kv_splits > 1 ? args.kv_splits : 1;
+  const int t0 = (int)(((long long)blockIdx.z * nkv_all) / nsplit);
+  const int nkv = (int)(((long long)(blockIdx.z + 1) * nkv_all) / nsplit) - t0;
   // Each CTA walks the K/V tiles starting from its own offset (step i reads
   // tile (i + kv0) mod nkv): the CTAs resident at one time then stream
   // different tiles instead of all requesting the same lines of L2 at once.
   // Online softmax is order-independent; the order is fixed per CTA, so
   // results stay deterministic.
   const int kv0 = (int)(((long long)blockIdx.x * nkv) / gridDim.x);
-  auto kv_tile = [&](int i) { const int t = i + kv0; return t >= nkv ? t - nkv : t; };
+  auto kv_tile = [&](int i) { const int t = i + kv0; return t0 + (t >= nkv ? t - nkv : t); };
   const int col0 = h * AT_D;
 
   if (threadIdx.x == 0) {
@@ -448,7 +453,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     // ring merge: both halves read the old (m, l) state before the pair
     // barrier, half 0 writes the new one after it
     float ms = 0.f, ls = 0.f;
-    const size_t si = (size_t)h * Tq + row;
+    const size_t si = (size_t)blockIdx.z * H * Tq + (size_t)h * Tq + row;
     if (MERGE && eok && row_ok && !args.first) {
       ms = args.m_state[si];
       ls = args.l_state[si];
@@ -503,7 +508,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           tmem_ld32(tO + cc * 32, u);
           tmem_wait_ld();
           if (row_ok) {
-            float4* op = reinterpret_cast<float4*>(args.o_acc + obase + cc * 32);
+            float4* op = reinterpret_cast<float4*>(args.o_acc + (size_t)blockIdx.z * Tq * H * AT_D + obase + cc * 32);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               float4 o = make_float4(__uint_as_float(u[4 * e]) * b, __uint_as_float(u[4 * e + 1]) * b,
@@ -531,21 +536,34 @@ done:
   }
 }
 
-// out = o_acc / l * gate (bf16), after the last ring step
-__global__ void attn_finalize_kernel(const float* __restrict__ o_acc, const float* __restrict__ l_state,
-                                     const float* __restrict__ gate, int ldg, int Tq, int H,
-                                     __nv_bfloat16* __restrict__ out) {
+// out = sum_z O_z 2^(m_z - m) / sum_z l_z 2^(m_z - m) * gate (bf16), m = max_z m_z:
+// the merge of `nsplit` partial states (m, l in log2 units), or with one state
+// the normalisation after the last ring step.
+__global__ void attn_combine_kernel(const float* __restrict__ o_acc, const float* __restrict__ m_state,
+                                    const float* __restrict__ l_state, int nsplit, const float* __restrict__ gate,
+                                    int ldg, int Tq, int H, __nv_bfloat16* __restrict__ out) {
   const size_t n = (size_t)Tq * H * (AT_D / 8);
+  const size_t ostride = (size_t)Tq * H * AT_D, sstride = (size_t)H * Tq;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const size_t e0 = i * 8;
     const int row = (int)(e0 / ((size_t)H * AT_D));
     const int h = (int)((e0 / AT_D) % H);
+    const size_t si = (size_t)h * Tq + row;
+    float m = m_state[si];
+    for (int z = 1; z < nsplit; ++z) m = fmaxf(m, m_state[z * sstride + si]);
+    float l = 0.f, o[8] = {};
+    for (int z = 0; z < nsplit; ++z) {
+      const float w = nsplit > 1 ? ex2_mufu(m_state[z * sstride + si] - m) : 1.0f;
+      l = fmaf(l_state[z * sstride + si], w, l);
+      const float4 a = reinterpret_cast<const float4*>(o_acc + z * ostride + e0)[0];
+      const float4 b = reinterpret_cast<const float4*>(o_acc + z * ostride + e0)[1];
+      o[0] = fmaf(a.x, w, o[0]); o[1] = fmaf(a.y, w, o[1]); o[2] = fmaf(a.z, w, o[2]); o[3] = fmaf(a.w, w, o[3]);
+      o[4] = fmaf(b.x, w, o[4]); o[5] = fmaf(b.y, w, o[5]); o[6] = fmaf(b.z, w, o[6]); o[7] = fmaf(b.w, w, o[7]);
+    }
     const float g = gate ? gate[(size_t)row * ldg + h] : 1.0f;
-    const float inv = g / l_state[(size_t)h * Tq + row];
-    const float4 a = reinterpret_cast<const float4*>(o_acc + e0)[0];
-    const float4 b = reinterpret_cast<const float4*>(o_acc + e0)[1];
-    reinterpret_cast<uint4*>(out + e0)[0] = make_uint4(pack_bf16x2(a.x * inv, a.y * inv), pack_bf16x2(a.z * inv, a.w * inv),
-                                                       pack_bf16x2(b.x * inv, b.y * inv), pack_bf16x2(b.z * inv, b.w * inv));
+    const float inv = g / l;
+    reinterpret_cast<uint4*>(out + e0)[0] = make_uint4(pack_bf16x2(o[0] * inv, o[1] * inv), pack_bf16x2(o[2] * inv, o[3] * inv),
+                                                       pack_bf16x2(o[4] * inv, o[5] * inv), pack_bf16x2(o[6] * inv, o[7] * inv));
   }
 }
 
@@ -565,7 +583,7 @@ static int launch_attn(const AttnArgs& a, cudaStream_t st) {
   if (!rc) rc = make_tmap_2d(&tk, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, a.Tkv, a.ldk, 64, AT_BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = make_tmap_2d(&tv, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, a.Tkv, a.ldv, 64, AT_BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  dim3 grid((a.Tq + 2 * AT_BM - 1) / (2 * AT_BM), a.H);
+  dim3 grid((a.Tq + 2 * AT_BM - 1) / (2 * AT_BM), a.H, MERGE && a.kv_splits > 1 ? a.kv_splits : 1);
   attn_tc_kernel<MERGE><<<grid, AT_THREADS, AT_SMEM, st>>>(tq, tk, tv, a);
   launched();
   cudaError_t e = cudaGetLastError();
@@ -592,16 +610,48 @@ cudaError_t attn_status(uint32_t* v, bool clear) {
   return e;
 }
 
-int attention_finalize(const AttnArgs& a, cudaStream_t st) {
+int attention_combine(const AttnArgs& a, cudaStream_t st) {
   const size_t n = (size_t)a.Tq * a.H * (AT_D / 8);
   if (n == 0) return LTXB_OK;
   int grid = (int)((n + 255) / 256);
   if (grid > 8 * sm_count()) grid = 8 * sm_count();
-  attn_finalize_kernel<<<grid, 256, 0, st>>>(a.o_acc, a.l_state, a.gate, a.ldg, a.Tq, a.H,
-                                             reinterpret_cast<__nv_bfloat16*>(a.out));
+  attn_combine_kernel<<<grid, 256, 0, st>>>(a.o_acc, a.m_state, a.l_state, a.kv_splits > 1 ? a.kv_splits : 1, a.gate,
+                                            a.ldg, a.Tq, a.H, reinterpret_cast<__nv_bfloat16*>(a.out));
   launched();
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "attention finalize");
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "attention combine");
+}
+
+int attention_kv_splits(int Tq, int Tkv, int H, int max_splits) {
+  // time ~ waves x tiles per split; a split adds one partial state to write
+  // and read back (about 3 % of a tile-sweep per split here)
+  const long long units = (long long)((Tq + 2 * AT_BM - 1) / (2 * AT_BM)) * H;
+  const int nkv = (Tkv + AT_BN - 1) / AT_BN, sms = sm_count();
+  int best = 1;
+  double best_t = 0;
+  for (int s = 1; s <= max_splits && s <= nkv; ++s) {
+    const double waves = (double)((units * s + sms - 1) / sms);
+    const double t = waves * ((nkv + s - 1) / s) * (1.0 + 0.03 * (s - 1));
+    if (s == 1 || t < best_t) {
+      best = s;
+      best_t = t;
+    }
+  }
+  return best;
+}
+
+int attention_split(AttnArgs a, int splits, cudaStream_t st) {
+  if (splits <= 1) {  // one range: the direct kernel writes the output itself
+    a.o_acc = a.m_state = a.l_state = nullptr;
+    a.kv_splits = 0;
+    return attention_tc(a, st);
+  }
+  if (!a.o_acc || !a.m_state || !a.l_state) return set_error(LTXB_EINVAL, "attention split: state buffers missing");
+  a.kv_splits = splits;
+  a.first = 1;
+  int rc = attention_tc(a, st);
+  if (rc) return rc;
+  return attention_combine(a, st);
 }
 
 }  // namespace ltxb

@@ -21,6 +21,7 @@
 //  14  h    = gelu(f . W1^T)                                  gemm  N = FF
 //  15  out  = x_ca + (h . W2^T) * ada5                        gemm  K = FF
 #include <nccl.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -248,6 +249,22 @@ struct Bufs {
 
 static bool g_fused_dequant = false;  // int8 GEMMs: dequantise in smem (true) or expand first (false)
 
+// Sequence-parallel self-attention: all-gather of K/V (default) or the ring
+// of send/recv steps (LTXB_SP_RING=1, kept for comparison).
+static bool sp_use_ring() {
+  static const bool ring = [] {
+    const char* e = getenv("LTXB_SP_RING");
+    return e && e[0] == '1';
+  }();
+  return ring;
+}
+// K/V splits of the gathered attention (1 for the ring, whose steps merge
+// into one state)
+static int sp_kv_splits(const ltxb_weights* w, const ltxb_config* c) {
+  if (sp_use_ring()) return 1;
+  return attention_kv_splits(c->T, c->T * c->sp_size, w->H, 4);
+}
+
 static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base, Bufs& b) {
   Ws ws;
   ws.base = base;
@@ -271,9 +288,10 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
   b.h = ws.take<uint8_t>(T * FF, act);
   if (w->mode == LTXB_MODE_INT8 && !g_fused_dequant) b.deq = ws.take<uint8_t>(FF * D, 2);
   if (c->sp_size > 1) {
-    b.o_acc = ws.take<float>(T * D);
-    b.m_st = ws.take<float>((size_t)w->H * T);
-    b.l_st = ws.take<float>((size_t)w->H * T);
+    const size_t ns = sp_kv_splits(w, c);
+    b.o_acc = ws.take<float>(ns * T * D);
+    b.m_st = ws.take<float>(ns * w->H * T);
+    b.l_st = ws.take<float>(ns * w->H * T);
   }
   return (ws.off + 255) & ~size_t(255);
 }
@@ -431,7 +449,45 @@ static int ring_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, 
     // (same stream). The last compute step waits on the last group, so the
     // comm stream is idle when the caller's stream is.
   }
-  return attention_finalize(a, st);
+  return attention_combine(a, st);
+}
+
+// All-gather variant: this rank's K (already in its slot) and V join the
+// other ranks' in one in-place ncclAllGather each (NVLink / NVSwitch
+// collective, all channels), then one split-K/V attention over the whole
+// sequence writes the gated output directly.
+static int sp_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* v_local,
+                        int ldv_local, const float* gate, cudaStream_t st) {
+  if (sp_use_ring()) return ring_attention(w, c, b, q, v_local, ldv_local, gate, st);
+  ltxb_comm* cm = c->comm;
+  const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D;
+  const size_t chunk = (size_t)T * D * 2;
+  uint8_t* kb = static_cast<uint8_t*>(b.k);
+  uint8_t* vb = static_cast<uint8_t*>(b.v);
+  cudaError_t e = cudaMemcpy2DAsync(vb + (size_t)r * chunk, (size_t)D * 2, v_local, (size_t)ldv_local * 2,
+                                    (size_t)D * 2, T, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return set_cuda_error(e, "sp: local V copy");
+  ncclGroupStart();
+  ncclAllGather(kb + (size_t)r * chunk, kb, chunk, ncclUint8, cm->nccl, st);
+  ncclAllGather(vb + (size_t)r * chunk, vb, chunk, ncclUint8, cm->nccl, st);
+  ncclResult_t nr = ncclGroupEnd();
+  if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "K/V all-gather: %s", ncclGetErrorString(nr));
+  AttnArgs a{};
+  a.q = q;
+  a.k = kb;
+  a.v = vb;
+  a.ldq = a.ldk = a.ldv = D;
+  a.out = b.o;
+  a.gate = gate;
+  a.ldg = w->G;
+  a.Tq = T;
+  a.Tkv = T * N;
+  a.H = w->H;
+  a.scale = 0.08838834764831845f;
+  a.o_acc = b.o_acc;
+  a.m_state = b.m_st;
+  a.l_state = b.l_st;
+  return attention_split(a, sp_kv_splits(w, c), st);
 }
 
 // The block, up to `stage` (LTXB_STAGE_BLOCK_OUT = whole block).
@@ -505,7 +561,7 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   {
     Phase p("attn_self", st);
     if (sp)
-      CK(ring_attention(w, c, b, b.q, col(b.qkv, 2 * D), 3 * D, g1, st));
+      CK(sp_attention(w, c, b, b.q, col(b.qkv, 2 * D), 3 * D, g1, st));
     else
       CK(attn(w, b.q, D, b.k, D, col(b.qkv, 2 * D), 3 * D, b.o, g1, T, T, st));
   }
@@ -881,6 +937,57 @@ int ltxb_attention(const void* q, const void* k, const void* v, void* out, const
   a.H = H;
   a.scale = scale;
   return attention_tc(a, static_cast<cudaStream_t>(stream));
+}
+
+static int split_count(int Tq, int Tkv, int H, int splits) {
+  const int nkv = (Tkv + 127) / 128;
+  if (splits <= 0) return attention_kv_splits(Tq, Tkv, H, 8);
+  return splits < nkv ? splits : nkv;
+}
+
+static uint64_t split_ws(int Tq, int H, int ns, size_t* o_off, size_t* m_off, size_t* l_off) {
+  auto up = [](uint64_t x) { return (x + 255) & ~uint64_t(255); };
+  const uint64_t ob = up((uint64_t)ns * Tq * H * 128 * 4), sb = up((uint64_t)ns * H * Tq * 4);
+  if (o_off) *o_off = 0;
+  if (m_off) *m_off = ob;
+  if (l_off) *l_off = ob + sb;
+  return ob + 2 * sb;
+}
+
+uint64_t ltxb_attention_split_workspace_bytes(int Tq, int Tkv, int H, int splits) {
+  if (Tq <= 0 || Tkv <= 0 || H <= 0) return 0;
+  return split_ws(Tq, H, split_count(Tq, Tkv, H, splits), nullptr, nullptr, nullptr);
+}
+
+int ltxb_attention_split(const void* q, const void* k, const void* v, void* out, const float* gate, int Tq, int Tkv,
+                         int H, float scale, int splits, void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (Tq <= 0) return LTXB_OK;
+  if (Tkv <= 0 || H <= 0) return set_error(LTXB_EINVAL, "attention split: empty K/V or no heads");
+  if (splits < 0) return set_error(LTXB_EINVAL, "attention split: negative split count");
+  const int ns = split_count(Tq, Tkv, H, splits);
+  size_t oo, mo, lo;
+  const uint64_t need = split_ws(Tq, H, ns, &oo, &mo, &lo);
+  if (!workspace || workspace_bytes < need)
+    return set_error(LTXB_EINVAL, "attention split: workspace of %llu bytes is smaller than the %llu required",
+                     (unsigned long long)workspace_bytes, (unsigned long long)need);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(LTXB_EINVAL, "workspace must be 256-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.ldq = a.ldk = a.ldv = H * 128;
+  a.out = out;
+  a.gate = gate;
+  a.ldg = H;
+  a.Tq = Tq;
+  a.Tkv = Tkv;
+  a.H = H;
+  a.scale = scale;
+  a.o_acc = reinterpret_cast<float*>(ws + oo);
+  a.m_state = reinterpret_cast<float*>(ws + mo);
+  a.l_state = reinterpret_cast<float*>(ws + lo);
+  return attention_split(a, ns, static_cast<cudaStream_t>(stream));
 }
 
 int ltxb_dq_gemm(const void* A, const void* Wq, const void* scales, int scale_dtype, const void* bias, void* out, int M,

@@ -92,9 +92,19 @@ struct AttnArgs {
   float* m_state;
   float* l_state;
   int first;  // state starts empty
+  // split-K/V: with kv_splits = s > 1 (and `first`), split z of s covers K/V
+  // tiles [z n / s, (z + 1) n / s) and writes its own state at o_acc + z Tq H
+  // 128, m/l + z H Tq; attention_combine merges the s states into `out`.
+  int kv_splits;
 };
 int attention_tc(const AttnArgs& a, cudaStream_t st);
-int attention_finalize(const AttnArgs& a, cudaStream_t st);
+// out = (merged state of a.kv_splits splits, 1 for a ring's accumulated state) / l * gate
+int attention_combine(const AttnArgs& a, cudaStream_t st);
+// split count that best fills the GPU's SMs for this shape (1 = no split)
+int attention_kv_splits(int Tq, int Tkv, int H, int max_splits);
+// whole split-K/V attention: partial states in (o_acc, m_state, l_state), sized for
+// attention_kv_splits(...) splits, then the combine into `out`
+int attention_split(AttnArgs a, int splits, cudaStream_t st);
 // status word of the attention unit (compiled separately, see common.cuh)
 cudaError_t attn_status(uint32_t* v, bool clear);
 

@@ -80,6 +80,8 @@ def _load() -> ctypes.CDLL:
         "ltxb_host_pipe_join": (i32, [vp, vp]),
         "ltxb_host_pipe_free": (None, [vp]),
         "ltxb_attention": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, f32, vp]),
+        "ltxb_attention_split_workspace_bytes": (u64, [i32, i32, i32, i32]),
+        "ltxb_attention_split": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, vp, u64, vp]),
         "ltxb_dq_gemm": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, vp, u64, vp]),
         "ltxb_gemm_bf16": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
     }
@@ -470,6 +472,22 @@ def attention(q, k, v, gate=None, scale: float | None = None, out=None, stream=N
     out = torch.empty_like(q) if out is None else out
     _check(lib.ltxb_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(gate), Tq, k.shape[0], H, float(scale),
                               _stream(stream)))
+    return out
+
+
+def attention_split(q, k, v, gate=None, splits: int = 0, scale: float | None = None, out=None, workspace=None,
+                    stream=None) -> torch.Tensor:
+    """attention() computed as `splits` K/V ranges merged afterwards (0 = the
+    library's choice for this GPU); for short query sequences."""
+    Tq, H, hd = q.shape
+    assert hd == 128 and q.dtype == torch.bfloat16
+    scale = 1.0 / np.sqrt(hd) if scale is None else scale
+    out = torch.empty_like(q) if out is None else out
+    need = lib.ltxb_attention_split_workspace_bytes(Tq, k.shape[0], H, int(splits))
+    if workspace is None:
+        workspace = torch.empty(max(int(need), 1), dtype=torch.uint8, device=q.device)
+    _check(lib.ltxb_attention_split(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(gate), Tq, k.shape[0], H,
+                                    float(scale), int(splits), _ptr(workspace), workspace.numel(), _stream(stream)))
     return out
 
 

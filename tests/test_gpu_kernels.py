@@ -145,6 +145,35 @@ def test_attention_config1_sampled(cuda):
     assert ref.rel_rms(out2[rows.to(cuda)].float().cpu(), want2) < ATTN_TOL
 
 
+@pytest.mark.parametrize("Tq,Tkv,H,splits", [(256, 1024, 2, 3), (300, 700, 3, 2), (130, 1000, 1, 8), (512, 2048, 4, 0),
+                                             (3520, 28160, 2, 0)])
+def test_attention_split(cuda, Tq, Tkv, H, splits):
+    """Split-K/V attention (partial states merged by the combine kernel)
+    against dense f64, and against the unsplit kernel."""
+    import ltxb
+    g = torch.Generator().manual_seed(Tq * 7 + Tkv)
+    q = torch.randn(Tq, H, 128, generator=g).to(cuda).to(torch.bfloat16)
+    k = torch.randn(Tkv, H, 128, generator=g).to(cuda).to(torch.bfloat16)
+    v = torch.randn(Tkv, H, 128, generator=g).to(cuda).to(torch.bfloat16)
+    gate = (2 * torch.sigmoid(torch.randn(Tq, H, generator=g))).to(cuda)
+    got = ltxb.attention_split(q, k, v, gate, splits=splits)
+    whole = ltxb.attention(q, k, v, gate)
+    torch.cuda.synchronize()
+    rows = torch.arange(0, Tq, max(1, Tq // 256))
+    want = _attn_ref(q[rows.to(cuda)], k, v, gate[rows.to(cuda)])
+    assert ref.rel_rms(got[rows.to(cuda)].float().cpu(), want) < ATTN_TOL
+    assert ref.rel_rms(got.float().cpu(), whole.float().cpu()) < 2 * ATTN_TOL  # two independent bf16-P roundings
+    assert ltxb.device_status() == ltxb.OK
+
+
+def test_attention_split_errors(cuda):
+    import ltxb
+    q = torch.zeros(64, 1, 128, device=cuda, dtype=torch.bfloat16)
+    small = torch.empty(16, dtype=torch.uint8, device=cuda)
+    with pytest.raises(ltxb.LtxbError):
+        ltxb.attention_split(q, q, q, splits=2, workspace=small)
+
+
 def test_attention_deterministic(cuda):
     import ltxb
     g = torch.Generator().manual_seed(9)

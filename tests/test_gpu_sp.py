@@ -1,4 +1,5 @@
-"""Multi-GPU test of the sequence-parallel block (ring attention over NCCL):
+"""Multi-GPU test of the sequence-parallel block (K/V all-gather + split-K/V
+attention by default, the send/recv ring with LTXB_SP_RING=1, over NCCL):
 tokens split across ranks, each rank holding its slice of x / tidx / RoPE
 tables; the gathered outputs must match the f64 oracle of the whole block and
 the single-GPU run of the library. Needs >= 2 GPUs (skipped otherwise).
@@ -20,8 +21,9 @@ pytestmark = pytest.mark.gpu
 D, FF, S = 256, 512, 16
 
 
-def _worker(rank, world, uid, grid, seed, mode, q):
+def _worker(rank, world, uid, grid, seed, mode, algo, q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["LTXB_SP_RING"] = "1" if algo == "ring" else "0"
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "ltx-zml_b200"), os.path.join(root, "tests")]
@@ -55,12 +57,12 @@ def _worker(rank, world, uid, grid, seed, mode, q):
         q.put((rank, None, False, -99, repr(exc)))
 
 
-def _run(world, grid, seed, mode):
+def _run(world, grid, seed, mode, algo="allgather"):
     import ltxb
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     uid = ltxb.Comm.unique_id()
-    procs = [ctx.Process(target=_worker, args=(r, world, uid, grid, seed, mode, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, uid, grid, seed, mode, algo, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -80,8 +82,9 @@ def _run(world, grid, seed, mode):
     return np.concatenate([res[r][0] for r in range(world)], axis=0)
 
 
+@pytest.mark.parametrize("algo", ["allgather", "ring"])
 @pytest.mark.parametrize("mode,grid", [("bf16", (2, 4, 32)), ("int8", (3, 4, 16))])
-def test_ring_block_matches_single_gpu_and_oracle(mode, grid):
+def test_sp_block_matches_single_gpu_and_oracle(mode, grid, algo):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     seed = 3
@@ -89,7 +92,7 @@ def test_ring_block_matches_single_gpu_and_oracle(mode, grid):
     geom, bw, data, ent, qset = helpers.weights_case(D, FF, seed, quant)
     inp = helpers.inputs_case(D, grid, S, seed, "axes", 3, "random")
     want = helpers.oracle_stages(bw, inp, qset if quant else None)["block_out"]
-    sp = _run(2, grid, seed, mode)
+    sp = _run(2, grid, seed, mode, algo)
     single = _run(1, grid, seed, mode)
     assert ref.rel_rms(sp, want) < 5e-3
     assert ref.rel_rms(single, want) < 5e-3
