@@ -165,6 +165,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const int warp = warp_id(), lane = lane_id();
   const int q0 = blockIdx.x * (2 * AT_BM), h = blockIdx.y;
   const int H = args.H, Tq = args.Tq, Tkv = args.Tkv;
+  const size_t ldo = args.ldo > 0 ? (size_t)args.ldo : (size_t)H * AT_D;  // output row stride (elements)
   // this CTA's K/V tiles: [t0, t0 + nkv) of the nkv_all tiles (one split of
   // kv_splits; the whole range without splitting)
   const int nkv_all = (Tkv + AT_BN - 1) / AT_BN;
@@ -474,7 +475,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           tmem_ld32(tO + cc * 32, u);
           tmem_wait_ld();
           if (row_ok) {
-            uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) + obase + cc * 32);
+            uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * ldo +
+                                                 h * AT_D + hf * 64 + cc * 32);
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               op[e] = make_uint4(pack_bf16x2(__uint_as_float(u[8 * e + 0]) * inv, __uint_as_float(u[8 * e + 1]) * inv),
@@ -541,7 +543,7 @@ done:
 // the normalisation after the last ring step.
 __global__ void attn_combine_kernel(const float* __restrict__ o_acc, const float* __restrict__ m_state,
                                     const float* __restrict__ l_state, int nsplit, const float* __restrict__ gate,
-                                    int ldg, int Tq, int H, __nv_bfloat16* __restrict__ out) {
+                                    int ldg, int Tq, int H, __nv_bfloat16* __restrict__ out, size_t ldo) {
   const size_t n = (size_t)Tq * H * (AT_D / 8);
   const size_t ostride = (size_t)Tq * H * AT_D, sstride = (size_t)H * Tq;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
@@ -562,7 +564,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ o_acc, const float
     }
     const float g = gate ? gate[(size_t)row * ldg + h] : 1.0f;
     const float inv = g / l;
-    reinterpret_cast<uint4*>(out + e0)[0] = make_uint4(pack_bf16x2(o[0] * inv, o[1] * inv), pack_bf16x2(o[2] * inv, o[3] * inv),
+    reinterpret_cast<uint4*>(out + (size_t)row * ldo + (e0 - (size_t)row * H * AT_D))[0] = make_uint4(pack_bf16x2(o[0] * inv, o[1] * inv), pack_bf16x2(o[2] * inv, o[3] * inv),
                                                        pack_bf16x2(o[4] * inv, o[5] * inv), pack_bf16x2(o[6] * inv, o[7] * inv));
   }
 }
@@ -616,7 +618,8 @@ int attention_combine(const AttnArgs& a, cudaStream_t st) {
   int grid = (int)((n + 255) / 256);
   if (grid > 8 * sm_count()) grid = 8 * sm_count();
   attn_combine_kernel<<<grid, 256, 0, st>>>(a.o_acc, a.m_state, a.l_state, a.kv_splits > 1 ? a.kv_splits : 1, a.gate,
-                                            a.ldg, a.Tq, a.H, reinterpret_cast<__nv_bfloat16*>(a.out));
+                                            a.ldg, a.Tq, a.H, reinterpret_cast<__nv_bfloat16*>(a.out),
+                                            a.ldo > 0 ? (size_t)a.ldo : (size_t)a.H * AT_D);
   launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "attention combine");

@@ -260,9 +260,12 @@ static bool sp_use_ring() {
 }
 // K/V splits of the gathered attention (1 for the ring, whose steps merge
 // into one state)
+// Head groups of the all-gather path: K/V travel and are attended group by
+// group, so that group g's attention overlaps the gathers of groups > g.
+static int sp_groups(const ltxb_weights* w) { return w->H % 4 == 0 ? 4 : 1; }
 static int sp_kv_splits(const ltxb_weights* w, const ltxb_config* c) {
   if (sp_use_ring()) return 1;
-  return attention_kv_splits(c->T, c->T * c->sp_size, w->H, 4);
+  return attention_kv_splits(c->T, c->T * c->sp_size, w->H / sp_groups(w), 8);
 }
 
 static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base, Bufs& b) {
@@ -288,10 +291,11 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
   b.h = ws.take<uint8_t>(T * FF, act);
   if (w->mode == LTXB_MODE_INT8 && !g_fused_dequant) b.deq = ws.take<uint8_t>(FF * D, 2);
   if (c->sp_size > 1) {
-    const size_t ns = sp_kv_splits(w, c);
-    b.o_acc = ws.take<float>(ns * T * D);
-    b.m_st = ws.take<float>(ns * w->H * T);
-    b.l_st = ws.take<float>(ns * w->H * T);
+    // split states of one head group (the ring: one state of all heads)
+    const size_t ns = sp_kv_splits(w, c), gh = sp_use_ring() ? w->H : w->H / sp_groups(w);
+    b.o_acc = ws.take<float>(ns * T * gh * 128);
+    b.m_st = ws.take<float>(ns * gh * T);
+    b.l_st = ws.take<float>(ns * gh * T);
   }
   return (ws.off + 255) & ~size_t(255);
 }
@@ -452,42 +456,68 @@ static int ring_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, 
   return attention_combine(a, st);
 }
 
-// All-gather variant: this rank's K (already in its slot) and V join the
-// other ranks' in one in-place ncclAllGather each (NVLink / NVSwitch
-// collective, all channels), then one split-K/V attention over the whole
-// sequence writes the gated output directly.
+// All-gather variant. The local K (in the attention-output buffer) and V
+// (in the fused q/k/v buffer) are regrouped into head-group-major gathered
+// buffers, [G][N T][D / G], so that each group's slice of every rank is one
+// contiguous block. Group by group, an in-place ncclAllGather on the
+// (high-priority) comm stream fills in the other ranks' K and V, and the
+// compute stream runs that group's split-K/V attention as soon as its gather
+// has landed: the gathers of later groups overlap the attention of earlier
+// ones.
 static int sp_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* v_local,
                         int ldv_local, const float* gate, cudaStream_t st) {
   if (sp_use_ring()) return ring_attention(w, c, b, q, v_local, ldv_local, gate, st);
   ltxb_comm* cm = c->comm;
   const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D;
-  const size_t chunk = (size_t)T * D * 2;
+  const int G = sp_groups(w), Dg = D / G, Hg = w->H / G;
+  if ((int)cm->ev.size() < G + 1) return set_error(LTXB_EINVAL, "sp: communicator event pool too small");
+  const size_t gbytes = (size_t)N * T * Dg * 2, sbytes = (size_t)T * Dg * 2;  // one group; one rank's slice
   uint8_t* kb = static_cast<uint8_t*>(b.k);
   uint8_t* vb = static_cast<uint8_t*>(b.v);
-  cudaError_t e = cudaMemcpy2DAsync(vb + (size_t)r * chunk, (size_t)D * 2, v_local, (size_t)ldv_local * 2,
-                                    (size_t)D * 2, T, cudaMemcpyDeviceToDevice, st);
-  if (e != cudaSuccess) return set_cuda_error(e, "sp: local V copy");
-  ncclGroupStart();
-  ncclAllGather(kb + (size_t)r * chunk, kb, chunk, ncclUint8, cm->nccl, st);
-  ncclAllGather(vb + (size_t)r * chunk, vb, chunk, ncclUint8, cm->nccl, st);
-  ncclResult_t nr = ncclGroupEnd();
-  if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "K/V all-gather: %s", ncclGetErrorString(nr));
-  AttnArgs a{};
-  a.q = q;
-  a.k = kb;
-  a.v = vb;
-  a.ldq = a.ldk = a.ldv = D;
-  a.out = b.o;
-  a.gate = gate;
-  a.ldg = w->G;
-  a.Tq = T;
-  a.Tkv = T * N;
-  a.H = w->H;
-  a.scale = 0.08838834764831845f;
-  a.o_acc = b.o_acc;
-  a.m_state = b.m_st;
-  a.l_state = b.l_st;
-  return attention_split(a, sp_kv_splits(w, c), st);
+  const uint8_t* kl = static_cast<const uint8_t*>(b.o);
+  const uint8_t* vl = static_cast<const uint8_t*>(v_local);
+  for (int g = 0; g < G; ++g) {
+    cudaError_t e = cudaMemcpy2DAsync(kb + g * gbytes + r * sbytes, (size_t)Dg * 2, kl + (size_t)g * Dg * 2,
+                                      (size_t)D * 2, (size_t)Dg * 2, T, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(vb + g * gbytes + r * sbytes, (size_t)Dg * 2, vl + (size_t)g * Dg * 2,
+                            (size_t)ldv_local * 2, (size_t)Dg * 2, T, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return set_cuda_error(e, "sp: regroup local K/V");
+  }
+  cudaEventRecord(cm->ev[0], st);
+  cudaStreamWaitEvent(cm->comm_stream, cm->ev[0], 0);
+  for (int g = 0; g < G; ++g) {
+    ncclGroupStart();
+    ncclAllGather(kb + g * gbytes + r * sbytes, kb + g * gbytes, sbytes, ncclUint8, cm->nccl, cm->comm_stream);
+    ncclAllGather(vb + g * gbytes + r * sbytes, vb + g * gbytes, sbytes, ncclUint8, cm->nccl, cm->comm_stream);
+    ncclResult_t nr = ncclGroupEnd();
+    if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "K/V all-gather, group %d: %s", g, ncclGetErrorString(nr));
+    cudaEventRecord(cm->ev[1 + g], cm->comm_stream);
+  }
+  const int ns = sp_kv_splits(w, c);
+  for (int g = 0; g < G; ++g) {
+    cudaStreamWaitEvent(st, cm->ev[1 + g], 0);
+    AttnArgs a{};
+    a.q = static_cast<const uint8_t*>(q) + (size_t)g * Dg * 2;
+    a.ldq = D;
+    a.k = kb + g * gbytes;
+    a.v = vb + g * gbytes;
+    a.ldk = a.ldv = Dg;
+    a.out = static_cast<uint8_t*>(b.o) + (size_t)g * Dg * 2;
+    a.ldo = D;
+    a.gate = gate ? gate + (size_t)g * Hg : nullptr;
+    a.ldg = w->G;
+    a.Tq = T;
+    a.Tkv = T * N;
+    a.H = Hg;
+    a.scale = 0.08838834764831845f;
+    a.o_acc = b.o_acc;  // states reused group after group (stream order)
+    a.m_state = b.m_st;
+    a.l_state = b.l_st;
+    int rc = attention_split(a, ns, st);
+    if (rc) return rc;
+  }
+  return LTXB_OK;
 }
 
 // The block, up to `stage` (LTXB_STAGE_BLOCK_OUT = whole block).
@@ -543,7 +573,9 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
     CK(run_lin(lc, w->g1, b.n, D, T, EPI_GATE2SIG_F32, b.gate, w->G));
   }
   // 4. q/k norm + RoPE (K goes to its slot of the gathered buffer under SP)
-  void* k_dst = col(b.k, (size_t)(sp ? c->sp_rank : 0) * T * D);
+  // (the all-gather path regroups K from the attention-output buffer, which
+  // is free until the attention writes it)
+  void* k_dst = !sp ? b.k : sp_use_ring() ? col(b.k, (size_t)c->sp_rank * T * D) : b.o;
   {
   Phase p("qk_norm_rope", st);
   if (f32) {
@@ -901,7 +933,9 @@ int ltxb_comm_init(const void* id, int rank, int nranks, int device, ltxb_comm**
     delete c;
     return set_error(LTXB_ENCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
   }
-  if (cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking) != cudaSuccess) {
+  int prio_lo = 0, prio_hi = 0;  // collectives get SMs ahead of queued compute blocks
+  cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi);
+  if (cudaStreamCreateWithPriority(&c->comm_stream, cudaStreamNonBlocking, prio_hi) != cudaSuccess) {
     ncclCommDestroy(c->nccl);
     delete c;
     return set_error(LTXB_ECUDA, "comm stream");

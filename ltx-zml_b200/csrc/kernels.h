@@ -80,7 +80,8 @@ struct AttnArgs {
   const void* k;  // bf16 [Tkv, H, 128], row stride ldk
   const void* v;  // bf16 [Tkv, H, 128], row stride ldv
   int ldq, ldk, ldv;
-  void* out;           // bf16 [Tq, H, 128] (contiguous)
+  void* out;           // bf16 [Tq, H, 128], row stride ldo elements (0: H * 128)
+  int ldo;
   const float* gate;   // f32 [Tq, ldg], column h = head h; or null
   int ldg;
   int Tq, Tkv, H;
