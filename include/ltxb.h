@@ -276,6 +276,68 @@ int ltxb_attention_split(const void* q, const void* k, const void* v, void* out,
 int ltxb_dq_gemm(const void* A, const void* Wq, const void* scales, int scale_dtype, const void* bias, void* out,
                  int M, int N, int K, int fused, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* RoPE tables on the device, in the block's cos/sin layout [T, H, 64] f32.
+ *  LTXB_ROPE_LTX: the reference's LTX layout (ltx/block_conformance.zig:87-127,
+ *    which replaces the host tables the harnesses load): pos = grid [3, T, 2]
+ *    f32 (start, end) per axis; frequencies theta^(k/(NF-1)) * pi/2 rounded
+ *    to f32, NF = H*128/6 (H <= 32); midpoint positions scaled to [-1, 1]
+ *    by max_pos (20, 2048, 2048); slot j = h*64 + f: j < 2 identity (1, 0),
+ *    else frequency (j-2)/3 of axis (j-2)%3.
+ *  LTXB_ROPE_AXES: the BASELINE configs' split of each head's 128 dims
+ *    into (44, 42, 42) per (frame, row, col) axis from integer positions
+ *    pos [T, 3] f32, the same table for every head.
+ * Angles and trigonometry in f64, rounded to f32 (as the reference's host
+ * generator; its gate allows 1-ulp stragglers in 0.01% of the values). */
+#define LTXB_ROPE_LTX 0
+#define LTXB_ROPE_AXES 1
+int ltxb_rope_tables(int kind, const float* pos, int T, int H, double theta, float* cos, float* sin, void* stream);
+
+/* ---- core parts: the steps either side of the blocks (ltx/core_parts.zig) ----
+ * f32 arithmetic with bf16 weights, like the reference's traced CoreParts.
+ * Weights come from a blob with the checkpoint's names (ltx/core_parts.zig:52-70):
+ * adaln_single.emb.timestep_embedder.linear_{1,2}.{weight,bias},
+ * adaln_single.linear.{weight,bias}, the same under prompt_adaln_single,
+ * patchify_proj.{weight,bias}, proj_out.{weight,bias} (bf16) and
+ * scale_shift_table [2, D] (f32). */
+typedef struct ltxb_core ltxb_core;
+int ltxb_core_upload(int device, const void* blob, uint64_t blob_bytes, const ltxb_entry* entries, int n_entries,
+                     int hidden, ltxb_core** out);
+void ltxb_core_free(ltxb_core* core);
+/* scratch for ltxb_core_adaln (K timesteps), ltxb_core_pts2 and ltxb_core_tail (T tokens) */
+uint64_t ltxb_core_workspace_bytes(const ltxb_core* core, int T, int K);
+/* out [K, 256] = cos | sin of t*1000*exp(i*(-ln 1e4)/128), f32 (core_parts.zig:42-49) */
+int ltxb_core_sinusoid(const float* t, int K, float* out, void* stream);
+/* t [K] -> embedded_timestep emb [K, D] (optional) and the block's ts9 table
+ * [K, 9, D] (CoreParts.emb / ts9r, core_parts.zig:117-137) */
+int ltxb_core_adaln(const ltxb_core* core, const float* t, int K, float* emb, float* ts9, void* workspace,
+                    uint64_t workspace_bytes, void* stream);
+/* sigma (one device float) -> pts2 [2, D] (CoreParts.pts2r, core_parts.zig:127-142) */
+int ltxb_core_pts2(const ltxb_core* core, const float* sigma, float* pts2, void* workspace, uint64_t workspace_bytes,
+                   void* stream);
+/* latent [T, 128] -> x [T, D] (patchify_proj, core_parts.zig:144-146) */
+int ltxb_core_patchify(const ltxb_core* core, const float* latent, int T, float* x, void* stream);
+/* velocity [T, 128] = proj_out(LayerNorm(x) * (1 + sst[1] + e) + sst[0] + e), e the RAW
+ * embedded_timestep of each token: emb[tidx[t]] (emb [K, D]), or emb [T, D] per token
+ * when tidx is NULL (CoreParts.tailFromEmb, core_parts.zig:148-170) */
+int ltxb_core_tail(const ltxb_core* core, const float* x, const float* emb, const int* tidx, int T, float* velocity,
+                   void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* ---- scheduler: the distilled LTX-2.5 sampler (ltx/scheduler.zig), bit-exact f32 ----
+ * Latents are [T, C] (C = 128 channels) with one mask / timestep value per token. */
+/* copies the sigma list of stage 1 (9 values) or 2 (4 values) into out (if not NULL);
+ * returns the count, or a negative status */
+int ltxb_sched_sigmas(int stage, float* out, int capacity);
+/* out = lerp(clean, lerp(clean, noise, noise_scale), mask) with torch.lerp's fused
+ * two-branch arithmetic (scheduler.zig:20-46) */
+int ltxb_sched_noise_init(const float* clean, const float* noise, const float* mask, int T, int C, float noise_scale,
+                          float* out, void* stream);
+/* ts = mask * sigma (scheduler.zig:49-51) */
+int ltxb_sched_timesteps(const float* mask, int T, float sigma, float* ts, void* stream);
+/* out = Euler step of x towards post_process(to_denoised(x, velocity, ts), clean, mask)
+ * from sigma to sigma_next (scheduler.zig:54-80, the host march of e2e_denoise.zig:320-325) */
+int ltxb_sched_step(const float* x, const float* velocity, const float* ts, const float* clean, const float* mask,
+                    int T, int C, float sigma, float sigma_next, float* out, void* stream);
+
 /* Size of the scratch ltxb_dq_gemm_noalloc keeps in the library image. */
 #define LTXB_NOALLOC_SCRATCH_BYTES (32u << 20)
 

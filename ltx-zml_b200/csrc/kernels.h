@@ -106,6 +106,9 @@ int attention_kv_splits(int Tq, int Tkv, int H, int max_splits);
 // whole split-K/V attention: partial states in (o_acc, m_state, l_state), sized for
 // attention_kv_splits(...) splits, then the combine into `out`
 int attention_split(AttnArgs a, int splits, cudaStream_t st);
+// RoPE tables (core.cu)
+int rope_tables(int kind, const float* pos, int T, int H, double theta, float* cos_out, float* sin_out,
+                cudaStream_t st);
 // status word of the attention unit (compiled separately, see common.cuh)
 cudaError_t attn_status(uint32_t* v, bool clear);
 

@@ -81,6 +81,19 @@ def _load() -> ctypes.CDLL:
         "ltxb_host_pipe_free": (None, [vp]),
         "ltxb_attention": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, f32, vp]),
         "ltxb_attention_split_workspace_bytes": (u64, [i32, i32, i32, i32]),
+        "ltxb_rope_tables": (i32, [i32, vp, i32, i32, ctypes.c_double, vp, vp, vp]),
+        "ltxb_core_upload": (i32, [i32, vp, u64, vp, i32, i32, ctypes.POINTER(vp)]),
+        "ltxb_core_free": (None, [vp]),
+        "ltxb_core_workspace_bytes": (u64, [vp, i32, i32]),
+        "ltxb_core_sinusoid": (i32, [vp, i32, vp, vp]),
+        "ltxb_core_adaln": (i32, [vp, vp, i32, vp, vp, vp, u64, vp]),
+        "ltxb_core_pts2": (i32, [vp, vp, vp, vp, u64, vp]),
+        "ltxb_core_patchify": (i32, [vp, vp, i32, vp, vp]),
+        "ltxb_core_tail": (i32, [vp, vp, vp, vp, i32, vp, vp, u64, vp]),
+        "ltxb_sched_sigmas": (i32, [i32, vp, i32]),
+        "ltxb_sched_noise_init": (i32, [vp, vp, vp, i32, i32, f32, vp, vp]),
+        "ltxb_sched_timesteps": (i32, [vp, i32, f32, vp, vp]),
+        "ltxb_sched_step": (i32, [vp, vp, vp, vp, vp, i32, i32, f32, f32, vp, vp]),
         "ltxb_attention_split": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, vp, u64, vp]),
         "ltxb_dq_gemm": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, vp, u64, vp]),
         "ltxb_gemm_bf16": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
@@ -268,6 +281,109 @@ def build_quant_bufs(blob: Blob, block_idx: int, qset: int = QSET_REF, hidden: i
                      device: int = 0) -> Weights:
     """ltx/loader.zig:158-172: int8 g128 pairs for the quantised linears."""
     return _upload(blob, block_idx, MODE_INT8, qset, hidden, ff, device)
+
+
+# ---------------------------------------------------------------------------
+# core parts and scheduler (ltx/core_parts.zig, ltx/scheduler.zig)
+# ---------------------------------------------------------------------------
+
+class Core:
+    """Device-resident core parts (`ltxb_core*`): CoreParts' methods on the GPU."""
+
+    def __init__(self, blob: Blob, hidden: int = 4096, device: int = 0):
+        host = np.frombuffer(blob.data, dtype=np.uint8)
+        arr, _keep = _entry_array(blob.manifest["entries"])
+        h = ctypes.c_void_p()
+        _check(lib.ltxb_core_upload(device, host.ctypes.data, host.size, ctypes.addressof(arr), len(arr), hidden,
+                                    ctypes.byref(h)))
+        self.handle, self.D, self.device = h, hidden, device
+
+    def free(self) -> None:
+        if self.handle:
+            lib.ltxb_core_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def _ws(self, T: int, K: int, dev):
+        n = lib.ltxb_core_workspace_bytes(self.handle, T, K)
+        return torch.empty(max(int(n), 1), dtype=torch.uint8, device=dev)
+
+    @staticmethod
+    def sinusoid(t, stream=None) -> torch.Tensor:
+        t = t.contiguous().float()
+        out = torch.empty(t.numel(), 256, dtype=torch.float32, device=t.device)
+        _check(lib.ltxb_core_sinusoid(_ptr(t), t.numel(), _ptr(out), _stream(stream)))
+        return out
+
+    def adaln(self, t, stream=None):
+        """t [K] -> (embedded_timestep [K, D], ts9 [K, 9, D])."""
+        t = t.contiguous().float()
+        K = t.numel()
+        emb = torch.empty(K, self.D, dtype=torch.float32, device=t.device)
+        ts9 = torch.empty(K, 9, self.D, dtype=torch.float32, device=t.device)
+        ws = self._ws(0, K, t.device)
+        _check(lib.ltxb_core_adaln(self.handle, _ptr(t), K, _ptr(emb), _ptr(ts9), _ptr(ws), ws.numel(),
+                                   _stream(stream)))
+        return emb, ts9
+
+    def pts2(self, sigma, stream=None) -> torch.Tensor:
+        """sigma (one-element device tensor) -> pts2 [2, D]."""
+        sigma = sigma.contiguous().float()
+        out = torch.empty(2, self.D, dtype=torch.float32, device=sigma.device)
+        ws = self._ws(0, 1, sigma.device)
+        _check(lib.ltxb_core_pts2(self.handle, _ptr(sigma), _ptr(out), _ptr(ws), ws.numel(), _stream(stream)))
+        return out
+
+    def patchify(self, latent, stream=None) -> torch.Tensor:
+        latent = latent.contiguous().float()
+        out = torch.empty(latent.shape[0], self.D, dtype=torch.float32, device=latent.device)
+        _check(lib.ltxb_core_patchify(self.handle, _ptr(latent), latent.shape[0], _ptr(out), _stream(stream)))
+        return out
+
+    def tail(self, x, emb, tidx=None, stream=None) -> torch.Tensor:
+        """tailFromEmb: x [T, D], emb [K, D] with tidx [T] (or emb [T, D]) -> velocity [T, 128]."""
+        T = x.shape[0]
+        out = torch.empty(T, 128, dtype=torch.float32, device=x.device)
+        ws = self._ws(T, 1, x.device)
+        _check(lib.ltxb_core_tail(self.handle, _ptr(x), _ptr(emb), _ptr(tidx), T, _ptr(out), _ptr(ws), ws.numel(),
+                                  _stream(stream)))
+        return out
+
+
+def sched_sigmas(stage: int) -> np.ndarray:
+    n = lib.ltxb_sched_sigmas(stage, None, 0)
+    if n < 0:
+        _check(n)
+    out = np.zeros(n, dtype=np.float32)
+    _check(min(0, lib.ltxb_sched_sigmas(stage, out.ctypes.data, n)))
+    return out
+
+
+def sched_noise_init(clean, noise, mask, noise_scale: float, out=None, stream=None) -> torch.Tensor:
+    T, C = clean.shape
+    out = torch.empty_like(clean) if out is None else out
+    _check(lib.ltxb_sched_noise_init(_ptr(clean), _ptr(noise), _ptr(mask), T, C, float(noise_scale), _ptr(out),
+                                     _stream(stream)))
+    return out
+
+
+def sched_timesteps(mask, sigma: float, out=None, stream=None) -> torch.Tensor:
+    out = torch.empty_like(mask) if out is None else out
+    _check(lib.ltxb_sched_timesteps(_ptr(mask), mask.numel(), float(sigma), _ptr(out), _stream(stream)))
+    return out
+
+
+def sched_step(x, velocity, ts, clean, mask, sigma: float, sigma_next: float, out=None, stream=None) -> torch.Tensor:
+    T, C = x.shape
+    out = torch.empty_like(x) if out is None else out
+    _check(lib.ltxb_sched_step(_ptr(x), _ptr(velocity), _ptr(ts), _ptr(clean), _ptr(mask), T, C, float(sigma),
+                               float(sigma_next), _ptr(out), _stream(stream)))
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -489,6 +605,22 @@ def attention_split(q, k, v, gate=None, splits: int = 0, scale: float | None = N
     _check(lib.ltxb_attention_split(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(gate), Tq, k.shape[0], H,
                                     float(scale), int(splits), _ptr(workspace), workspace.numel(), _stream(stream)))
     return out
+
+
+ROPE_LTX = 0
+ROPE_AXES = 1
+
+
+def rope_tables(kind: int, pos, n_heads: int, theta: float = 10000.0, stream=None):
+    """cos, sin [T, H, 64] f32 on pos's device. ROPE_LTX: pos = grid [3, T, 2]
+    (start, end) f32; ROPE_AXES: pos = [T, 3] (frame, row, col) f32."""
+    pos = pos.contiguous().float()
+    T = pos.shape[1] if kind == ROPE_LTX else pos.shape[0]
+    cos = torch.empty(T, n_heads, 64, dtype=torch.float32, device=pos.device)
+    sin = torch.empty_like(cos)
+    _check(lib.ltxb_rope_tables(int(kind), _ptr(pos), T, n_heads, float(theta), _ptr(cos), _ptr(sin),
+                                _stream(stream)))
+    return cos, sin
 
 
 def dq_gemm(a, wq, scales, bias=None, fused: bool = True, out=None, workspace=None, stream=None) -> torch.Tensor:
