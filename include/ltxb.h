@@ -205,7 +205,8 @@ uint64_t ltxb_block_workspace_bytes(const ltxb_weights* w, const ltxb_config* cf
 /* out = block(x): the whole block, blockwise (flash) self-attention. The
  * equivalent of exe.call on `wBlockOut` / `qBlockOutAll`
  * (ltx/e2e_prod.zig:377-395). With sp_size > 1 the ranks exchange K/V
- * shards over NVLink (ring attention); each rank holds its token slice. */
+ * over NVLink (a head-group pipelined all-gather; the send/recv ring with
+ * the environment variable LTXB_SP_RING=1); each rank holds its token slice. */
 int ltxb_block_forward(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_config* cfg, void* stream);
 
 /* One conformance stage (LTXB_STAGE_*) of the block, written to stage_out
@@ -337,6 +338,33 @@ int ltxb_sched_timesteps(const float* mask, int T, float sigma, float* ts, void*
  * from sigma to sigma_next (scheduler.zig:54-80, the host march of e2e_denoise.zig:320-325) */
 int ltxb_sched_step(const float* x, const float* velocity, const float* ts, const float* clean, const float* mask,
                     int T, int C, float sigma, float sigma_next, float* out, void* stream);
+
+/* ---- the denoising loop (ltx/e2e_denoise.zig:218-336) on the device ----
+ * Per step s (sigma = sigmas[s], sigma_next = sigmas[s+1]): ts = mask*sigma;
+ * t_k = mask_values[k]*sigma -> embedded_timestep [K, D] and ts9 [K, 9, D];
+ * pts2 from sigma; x = patchify(latent); x = block_b(x) for every block;
+ * velocity = tail(x, embedded_timestep[tidx]); latent = Euler step of
+ * latent towards post_process(to_denoised(latent, velocity, ts)). Latents,
+ * tables and activations stay on the device; nothing synchronises the host.
+ * cfg.T is this rank's tokens, cfg.K the number of distinct mask values;
+ * with cfg.sp_size > 1 each rank passes its token slice (latent, clean, mask,
+ * tidx, cos, sin) and the blocks exchange K/V as in ltxb_block_forward. */
+typedef struct {
+  float* latent;             /* [T, 128] f32: the noised initial latent in, the final latent out */
+  const float* clean;        /* [T, 128] clean latent (the post-process blend)                     */
+  const float* mask;         /* [T] denoise mask                                                   */
+  const float* mask_values;  /* [K] its distinct values                                            */
+  const int32_t* tidx;       /* [T] index of each token's mask value in mask_values                */
+  const float* ctx;          /* [S, D] text context                                                */
+  const float* cos;          /* [T, H, 64] RoPE tables                                             */
+  const float* sin;
+  void* workspace;           /* ltxb_denoise_workspace_bytes, 256-byte aligned                     */
+  uint64_t workspace_bytes;
+} ltxb_denoise_io;
+uint64_t ltxb_denoise_workspace_bytes(const ltxb_core* core, const ltxb_weights* block, const ltxb_config* cfg);
+/* sigmas: host array of n_steps + 1 values (e.g. ltxb_sched_sigmas(1, ...): 8 steps) */
+int ltxb_denoise_run(const ltxb_core* core, const ltxb_weights* const* blocks, int n_blocks, const float* sigmas,
+                     int n_steps, const ltxb_denoise_io* io, const ltxb_config* cfg, void* stream);
 
 /* Size of the scratch ltxb_dq_gemm_noalloc keeps in the library image. */
 #define LTXB_NOALLOC_SCRATCH_BYTES (32u << 20)

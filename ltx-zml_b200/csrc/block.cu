@@ -83,7 +83,8 @@ struct Bufs {
   void* k2 = nullptr;     // [S, D]
   float* x_ca = nullptr;  // [T, D]
   void* h = nullptr;      // [T, FF]
-  void* deq = nullptr;    // [FF * D] bf16: int8 weights expanded (unfused int8 path)
+  void* deq = nullptr;    // bf16: the int8 weights of one linear expanded (unfused int8 path)
+  size_t deq_elems = 0;   // its capacity in elements
   float* o_acc = nullptr; // [T, D]  ring state
   float* m_st = nullptr;  // [H, T]
   float* l_st = nullptr;  // [H, T]
@@ -131,7 +132,11 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
   b.k2 = ws.take<uint8_t>(S * D, act);
   b.x_ca = ws.take<float>(T * D);
   b.h = ws.take<uint8_t>(T * FF, act);
-  if (w->mode == LTXB_MODE_INT8 && !g_fused_dequant) b.deq = ws.take<uint8_t>(FF * D, 2);
+  if (w->mode == LTXB_MODE_INT8 && !g_fused_dequant) {
+    // the largest int8 matrix expanded at once: the fused q/k/v [3D, D] or an FFN one [FF, D]
+    b.deq = ws.take<uint8_t>(std::max(FF * D, 3 * D * D), 2);
+    b.deq_elems = std::max(FF * D, 3 * D * D);
+  }
   if (c->sp_size > 1) {
     // split states of one head group (the ring: one state of all heads)
     const size_t ns = sp_kv_splits(w, c), gh = sp_use_ring() ? w->H : w->H / sp_groups(w);
@@ -188,6 +193,8 @@ static int run_lin(const LinCall& lc, const Lin& L, const void* A, int lda, int 
       g.scales = L.sc;
       g.scale_bf16 = L.sc_bf16;
     } else {
+      if ((size_t)L.N * L.K > lc.b->deq_elems)
+        return set_error(LTXB_EINVAL, "int8 linear [%d, %d] exceeds the expansion buffer", L.N, L.K);
       int rc = dequant_weights(L.wq, L.sc, L.sc_bf16, L.N, L.K, lc.b->deq, lc.st);
       if (rc) return rc;
       g.B = lc.b->deq;

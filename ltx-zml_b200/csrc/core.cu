@@ -198,6 +198,10 @@ static int silu(const float* x, float* y, size_t n, cudaStream_t st) {
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "silu");
 }
 
+__global__ void fill_kernel(float* p, int n, float v) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = v;
+}
+
 // ---------------------------------------------------------------------------
 // scheduler
 // ---------------------------------------------------------------------------
@@ -419,6 +423,95 @@ int ltxb_sched_step(const float* x, const float* velocity, const float* ts, cons
   launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "scheduler step");
+}
+
+// ---------------------------------------------------------------------------
+// denoising loop
+// ---------------------------------------------------------------------------
+
+struct DenoiseWs {
+  uint8_t* block;  // the blocks' workspace
+  float *x, *emb, *ts9, *pts2, *vel, *ts, *tk, *sig, *core;
+  uint64_t block_bytes, core_bytes, total;
+};
+
+static DenoiseWs denoise_layout(const ltxb_core* c, const ltxb_weights* blk, const ltxb_config* cfg, uint8_t* base) {
+  DenoiseWs w{};
+  const uint64_t T = cfg->T, K = cfg->K, D = c->D;
+  uint64_t off = 0;
+  auto take = [&](uint64_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += up256(bytes);
+    return p;
+  };
+  w.block_bytes = ltxb_block_workspace_bytes(blk, cfg);
+  w.core_bytes = ltxb_core_workspace_bytes(c, cfg->T, cfg->K);
+  w.block = take(w.block_bytes);
+  w.x = reinterpret_cast<float*>(take(T * D * 4));
+  w.emb = reinterpret_cast<float*>(take(K * D * 4));
+  w.ts9 = reinterpret_cast<float*>(take(K * 9 * D * 4));
+  w.pts2 = reinterpret_cast<float*>(take(2 * D * 4));
+  w.vel = reinterpret_cast<float*>(take(T * 128 * 4));
+  w.ts = reinterpret_cast<float*>(take(T * 4));
+  w.tk = reinterpret_cast<float*>(take(K * 4));
+  w.sig = reinterpret_cast<float*>(take(4));
+  w.core = reinterpret_cast<float*>(take(w.core_bytes));
+  w.total = off;
+  return w;
+}
+
+uint64_t ltxb_denoise_workspace_bytes(const ltxb_core* core, const ltxb_weights* block, const ltxb_config* cfg) {
+  if (!core || !block || !cfg) return 0;
+  return denoise_layout(core, block, cfg, nullptr).total;
+}
+
+int ltxb_denoise_run(const ltxb_core* core, const ltxb_weights* const* blocks, int n_blocks, const float* sigmas,
+                     int n_steps, const ltxb_denoise_io* io, const ltxb_config* cfg, void* stream) {
+  if (!core || !blocks || n_blocks <= 0 || !sigmas || n_steps < 0 || !io || !cfg)
+    return set_error(LTXB_EINVAL, "denoise: null argument");
+  if (!io->latent || !io->clean || !io->mask || !io->mask_values || !io->tidx || !io->ctx || !io->cos || !io->sin)
+    return set_error(LTXB_EINVAL, "denoise: null tensor");
+  if (cfg->T <= 0 || cfg->K <= 0 || cfg->S <= 0) return set_error(LTXB_EINVAL, "denoise: T, K and S must be positive");
+  for (int b = 0; b < n_blocks; ++b)
+    if (!blocks[b]) return set_error(LTXB_EINVAL, "denoise: block %d is null", b);
+  const DenoiseWs need = denoise_layout(core, blocks[0], cfg, nullptr);
+  if (!io->workspace || io->workspace_bytes < need.total)
+    return set_error(LTXB_EINVAL, "denoise: workspace of %llu bytes is smaller than the %llu required",
+                     (unsigned long long)io->workspace_bytes, (unsigned long long)need.total);
+  if (reinterpret_cast<uintptr_t>(io->workspace) & 255) return set_error(LTXB_EINVAL, "workspace must be 256-byte aligned");
+  const DenoiseWs w = denoise_layout(core, blocks[0], cfg, static_cast<uint8_t*>(io->workspace));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int T = cfg->T, K = cfg->K;
+  ltxb_block_io bio{};
+  bio.x = w.x;
+  bio.out = w.x;  // the block allows out == x
+  bio.tstab = w.ts9;
+  bio.tidx = io->tidx;
+  bio.ctx = io->ctx;
+  bio.pts2 = w.pts2;
+  bio.cos = io->cos;
+  bio.sin = io->sin;
+  bio.workspace = w.block;
+  bio.workspace_bytes = w.block_bytes;
+  int rc;
+  for (int s = 0; s < n_steps; ++s) {
+    const float sigma = sigmas[s], sigma_next = sigmas[s + 1];
+    // conditioning: per-token ts, per-mask-value t_k (the same f32 products)
+    if ((rc = ltxb_sched_timesteps(io->mask, T, sigma, w.ts, st))) return rc;
+    if ((rc = ltxb_sched_timesteps(io->mask_values, K, sigma, w.tk, st))) return rc;
+    fill_kernel<<<1, 32, 0, st>>>(w.sig, 1, sigma);  // sigma as a device scalar for pts2
+    launched();
+    if ((rc = ltxb_core_adaln(core, w.tk, K, w.emb, w.ts9, w.core, w.core_bytes, st))) return rc;
+    if ((rc = ltxb_core_pts2(core, w.sig, w.pts2, w.core, w.core_bytes, st))) return rc;
+    if ((rc = ltxb_core_patchify(core, io->latent, T, w.x, st))) return rc;
+    for (int b = 0; b < n_blocks; ++b)
+      if ((rc = ltxb_block_forward(blocks[b], &bio, cfg, st))) return rc;
+    if ((rc = ltxb_core_tail(core, w.x, w.emb, io->tidx, T, w.vel, w.core, w.core_bytes, st))) return rc;
+    if ((rc = ltxb_sched_step(io->latent, w.vel, w.ts, io->clean, io->mask, T, 128, sigma, sigma_next, io->latent, st)))
+      return rc;
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "denoise loop");
 }
 
 }  // extern "C"

@@ -91,6 +91,8 @@ def _load() -> ctypes.CDLL:
         "ltxb_core_patchify": (i32, [vp, vp, i32, vp, vp]),
         "ltxb_core_tail": (i32, [vp, vp, vp, vp, i32, vp, vp, u64, vp]),
         "ltxb_sched_sigmas": (i32, [i32, vp, i32]),
+        "ltxb_denoise_workspace_bytes": (u64, [vp, vp, vp]),
+        "ltxb_denoise_run": (i32, [vp, vp, i32, vp, i32, vp, vp, vp]),
         "ltxb_sched_noise_init": (i32, [vp, vp, vp, i32, i32, f32, vp, vp]),
         "ltxb_sched_timesteps": (i32, [vp, i32, f32, vp, vp]),
         "ltxb_sched_step": (i32, [vp, vp, vp, vp, vp, i32, i32, f32, f32, vp, vp]),
@@ -434,6 +436,33 @@ class _IO(ctypes.Structure):
                 ("tidx", ctypes.c_void_p), ("ctx", ctypes.c_void_p), ("pts2", ctypes.c_void_p),
                 ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
                 ("workspace_bytes", ctypes.c_uint64)]
+
+
+class _DenoiseIO(ctypes.Structure):
+    _fields_ = [("latent", ctypes.c_void_p), ("clean", ctypes.c_void_p), ("mask", ctypes.c_void_p),
+                ("mask_values", ctypes.c_void_p), ("tidx", ctypes.c_void_p), ("ctx", ctypes.c_void_p),
+                ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
+                ("workspace_bytes", ctypes.c_uint64)]
+
+
+def denoise(core: "Core", blocks: list, sigmas, latent, clean, mask, mask_values, tidx, ctx, cos, sin,
+            comm: "Comm | None" = None, stream=None):
+    """The denoising loop of ltx/e2e_denoise.zig:218-336 on the device
+    (ltxb_denoise_run): len(sigmas) - 1 steps over all `blocks`; `latent`
+    [T, 128] f32 is updated in place and returned."""
+    sig = np.ascontiguousarray(np.asarray(sigmas, dtype=np.float32))
+    T = latent.shape[0]
+    w0 = blocks[0]
+    cfg = _Config(T, ctx.shape[0], mask_values.numel(), w0.mode, comm.rank if comm else 0,
+                  comm.nranks if comm else 1, comm.handle if comm else None)
+    need = lib.ltxb_denoise_workspace_bytes(core.handle, w0.handle, ctypes.byref(cfg))
+    ws = torch.empty(int(need), dtype=torch.uint8, device=latent.device)
+    io = _DenoiseIO(_ptr(latent), _ptr(clean), _ptr(mask), _ptr(mask_values), _ptr(tidx), _ptr(ctx), _ptr(cos),
+                    _ptr(sin), _ptr(ws), ws.numel())
+    handles = (ctypes.c_void_p * len(blocks))(*[b.handle for b in blocks])
+    _check(lib.ltxb_denoise_run(core.handle, handles, len(blocks), sig.ctypes.data, len(sig) - 1, ctypes.byref(io),
+                                ctypes.byref(cfg), _stream(stream)))
+    return latent
 
 
 class Block:

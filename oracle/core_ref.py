@@ -201,3 +201,29 @@ def scheduler_step(x, vel, ts, clean, mask, sigma: float, sigma_next: float) -> 
     den = to_denoised(x, vel, ts)
     post = post_process(den, clean, mask)
     return euler_step(x, post, sigma, sigma_next)
+
+
+def denoise_ref(core: CoreParts, blocks: list, sigmas, latent, clean, mask, mask_values, tidx, ctx, cos, sin,
+                dtype=torch.float64) -> list:
+    """The loop of ltx/e2e_denoise.zig:218-336: per step, conditioning from
+    the f32 timesteps, patchify, every block, the tail, then the f32 host
+    march. Core parts and blocks in `dtype`; returns the latent after each
+    step (f32)."""
+    out = []
+    lat = np.asarray(latent, dtype=np.float32)
+    c = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dtype)
+    tid = torch.from_numpy(np.asarray(tidx, dtype=np.int32))
+    for s in range(len(sigmas) - 1):
+        sg, sn = float(sigmas[s]), float(sigmas[s + 1])
+        ts = timesteps(mask, sg)
+        tk = timesteps(mask_values, sg)
+        emb = core.emb(tk).to(dtype)
+        ts9 = core.ts9r(tk).to(dtype)
+        pts2 = core.pts2r(sg).to(dtype)
+        x = core.patchify(c(lat)).to(dtype)
+        for b in blocks:
+            x = b.block_out(x, ts9, tid, c(ctx), pts2, c(cos), c(sin))
+        vel = core.tail_from_emb(x.double(), emb.double()[tid.long()]).numpy().astype(np.float32)
+        lat = scheduler_step(lat, vel, ts, clean, mask, sg, sn)
+        out.append(lat)
+    return out

@@ -170,3 +170,22 @@ def test_host_pipe_matches_device_forward(cuda):
         torch.cuda.synchronize()
         assert torch.equal(oi, want.cpu())
     pipe.free()
+
+
+def test_workspace_is_not_overrun(cuda):
+    """The block stays inside ltxb_block_workspace_bytes: a guard region
+    after the workspace is untouched (int8 with FF < 3 D, where the fused
+    q/k/v matrix is the largest one expanded)."""
+    import ltxb
+    geom, bw, data, ent, _ = helpers.weights_case(SMALL["d"], SMALL["ff"], 2, "int8")
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 2, "axes", 3, "random")
+    w = helpers.upload(data, ent, geom, ltxb.MODE_INT8)
+    blk = ltxb.QBlock(w)
+    t = helpers.to_cuda(inp, cuda)
+    need = blk.workspace_bytes(t[0].shape[0], t[3].shape[0], t[1].shape[0])
+    guard = 1 << 20
+    blk._ws = torch.full((need + 256 + guard,), 0xA5, dtype=torch.uint8, device=cuda)
+    start = ((blk._ws.data_ptr() + 255) & ~255) - blk._ws.data_ptr()
+    blk.forward(*t)
+    torch.cuda.synchronize()
+    assert bool((blk._ws[start + need:] == 0xA5).all())

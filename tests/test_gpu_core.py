@@ -157,3 +157,65 @@ def test_scheduler_bit_exact(cuda):
         want = cr.scheduler_step(x, vel, ts, clean, mask, s, sn)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"step {i}"
         x = want
+
+
+# ---------------------------------------------------------------------------
+# the denoising loop
+# ---------------------------------------------------------------------------
+
+import helpers
+
+
+@pytest.mark.parametrize("mode", ["f32", "int8"])
+def test_denoise_loop_matches_oracle_trajectory(cuda, mode):
+    """Three distilled steps over two blocks at D 256 (ltx/e2e_denoise.zig's
+    loop): the latent after each step against the oracle's trajectory (core
+    parts and blocks in f64, scheduler bit-exact f32). f32 blocks: rel-RMS
+    1e-5. int8 blocks: the reference's per-step 2e-3 gate
+    (ltx/e2e_denoise.zig:310-333), or the error of the same loop with the
+    blocks in torch bf16 where that floor is higher."""
+    import ltxb
+    d, ff, grid = 256, 512, (2, 4, 8)
+    T = grid[0] * grid[1] * grid[2]
+    quant = "int8" if mode == "int8" else None
+    blocks_o, blocks_g, bws = [], [], []
+    for i in range(2):
+        geom, bw, data, ent, qset = helpers.weights_case(d, ff, 20 + i, quant)
+        bws.append((bw, qset))
+        blocks_o.append(ref.QBlock(bw, torch.float64, qset=qset) if quant else ref.Block(bw, torch.float64))
+        blocks_g.append(helpers.upload(data, ent, geom, ltxb.MODE_INT8 if quant else ltxb.MODE_F32))
+    cw, core = _core(d, 5)
+    inp = helpers.inputs_case(d, grid, 16, 4, "axes", 1, "random")
+    rng = np.random.default_rng(9)
+    clean = rng.standard_normal((T, 128)).astype(np.float32)
+    noise = rng.standard_normal((T, 128)).astype(np.float32)
+    mask_values = np.array([1.0, 0.5], dtype=np.float32)
+    tidx = (np.arange(T) % 7 == 0).astype(np.int32)   # a few half-denoised tokens
+    mask = mask_values[tidx]
+    lat0 = cr.noise_init(clean, noise, mask, 1.0)
+    sig = ltxb.sched_sigmas(1)[:4]
+    want = cr.denoise_ref(cr.CoreParts(cw), blocks_o, sig, lat0, clean, mask, mask_values, tidx, inp.ctx,
+                          inp.cos, inp.sin)
+    g = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    got = []
+    lat = g(lat0)
+    for s in range(3):
+        ltxb.denoise(core, blocks_g, sig[s:s + 2], lat, g(clean), g(mask), g(mask_values), g(tidx), g(inp.ctx),
+                     g(inp.cos), g(inp.sin))
+        got.append(lat.cpu().numpy().copy())
+    lat_all = g(lat0)
+    ltxb.denoise(core, blocks_g, sig, lat_all, g(clean), g(mask), g(mask_values), g(tidx), g(inp.ctx), g(inp.cos),
+                 g(inp.sin))
+    torch.cuda.synchronize()
+    assert ltxb.device_status() == ltxb.OK
+    if mode == "f32":
+        tol = [1e-5] * 3
+    else:
+        # the bf16 deployment floor: the same loop with the blocks run in torch bf16
+        b16_blocks = [ref.QBlock(bw, torch.bfloat16, qset=qs) for bw, qs in bws]
+        b16 = cr.denoise_ref(cr.CoreParts(cw), b16_blocks, sig, lat0, clean, mask, mask_values, tidx, inp.ctx,
+                             inp.cos, inp.sin, dtype=torch.bfloat16)
+        tol = [max(2e-3, ref.rel_rms(b16[s], want[s])) for s in range(3)]
+    for s in range(3):
+        assert ref.rel_rms(got[s], want[s]) <= tol[s], (s, ref.rel_rms(got[s], want[s]), tol[s])
+    assert np.array_equal(lat_all.cpu().numpy(), got[-1])  # one 3-step call == three 1-step calls
