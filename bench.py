@@ -139,30 +139,26 @@ class ClockSampler:
 # synthetic config-3 block, generated on the GPU
 # ---------------------------------------------------------------------------
 
-QUANT_FIELDS = ("q1_w", "k1_w", "v1_w", "o1_w", "q2_w", "k2_w", "v2_w", "o2_w", "ff1_w", "ff2_w")
-
-
-def make_blob(device, seed: int = 0):
+def make_blob(device, seed: int = 0, block: int = 0):
     """Config-3 weights: N(0, 0.02) (norm weights 1 + N(0, 0.02), tables f32),
-    int8 g128 for QUANT_FIELDS after scaling 0.5% of input channels x20,
+    int8 g128 for the extended set (q/k/v/o of both attentions and the FFN)
+    after scaling 0.5% of input channels x20,
     symmetric absmax/127 scales rounded to bf16; packed in the reference blob
-    format (name-sorted, 64-byte aligned)."""
-    from oracle import blob as oblob
-    from oracle import ltx_block_ref as ref
-    geom = ref.Geometry(d=D, ff=FF)
+    format (name-sorted, 64-byte aligned) by the library's writer."""
+    from ltxb import blobfmt
     g = torch.Generator(device=device)
     tensors = []
-    for i, (field, _stem, dims) in enumerate(ref.WEIGHT_SPECS):
-        shape = geom.dims(dims)
+    for i, (suffix, spec, dt) in enumerate(blobfmt.BLOCK_TENSORS):
+        shape = blobfmt.shape_of(spec, D, FF)
         g.manual_seed(seed * 1000 + i)
         w = torch.randn(*shape, generator=g, device=device) * 0.02
-        name = f"transformer_blocks.0.{oblob.DOTTED[field]}"
-        if field in ref.F32_FIELDS:
-            tensors.append((name, "F32", list(shape), w.cpu().numpy().tobytes()))
+        name = f"transformer_blocks.{block}.{suffix}"
+        if dt == "F32":
+            tensors.append((name, "F32", shape, w.cpu().numpy().tobytes()))
             continue
-        if field.startswith(("qn", "kn")):
+        if "norm" in suffix:
             w = w + 1.0
-        if field in QUANT_FIELDS:
+        if suffix in blobfmt.Q8_EXT:
             k = shape[1]
             cols = torch.randperm(k, generator=g, device=device)[: max(1, round(0.005 * k))]
             w[:, cols] *= 20.0
@@ -170,14 +166,13 @@ def make_blob(device, seed: int = 0):
             amax = wg.abs().amax(-1, keepdim=True)
             sc = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax)).to(torch.bfloat16)
             q = torch.clamp(torch.round(wg / sc.float()), -128, 127).to(torch.int8).view(shape)
-            tensors.append((name + "::q8", "I8", list(shape), q.cpu().numpy().tobytes()))
+            tensors.append((name + "::q8", "I8", shape, q.cpu().numpy().tobytes()))
             tensors.append((name + "::q8scale", "BF16", [shape[0], k // 128],
                             sc.view(torch.int16).view(shape[0], k // 128).cpu().numpy().tobytes()))
         else:
-            tensors.append((name, "BF16", list(shape), w.to(torch.bfloat16).view(torch.int16).cpu().numpy().tobytes()))
-    data, entries = oblob.pack(tensors)
-    ent = [dict(name=e.name, dtype=e.dtype, shape=e.shape, offset=e.offset, nbytes=e.nbytes) for e in entries]
-    return data, ent
+            tensors.append((name, "BF16", shape, w.to(torch.bfloat16).view(torch.int16).cpu().numpy().tobytes()))
+    data, entries = blobfmt.pack(tensors)
+    return data, entries
 
 
 def make_inputs(device, rank: int, world: int, seed: int = 0):
@@ -420,6 +415,103 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# the denoising loop (an extra measurement, not the driver's metric)
+# ---------------------------------------------------------------------------
+
+def make_core_blob(device, seed: int = 0):
+    """Core-part weights N(0, 0.02) (bf16; scale_shift_table f32) in the blob format."""
+    from ltxb import blobfmt
+    g = torch.Generator(device=device)
+    tensors = []
+    for i, (name, spec, dt) in enumerate(blobfmt.CORE_TENSORS):
+        shape = blobfmt.shape_of(spec, D)
+        g.manual_seed(seed * 1000 + 500 + i)
+        w = torch.randn(*shape, generator=g, device=device) * 0.02
+        raw = w.cpu().numpy() if dt == "F32" else w.to(torch.bfloat16).view(torch.int16).cpu().numpy()
+        tensors.append((name, dt, shape, raw.tobytes()))
+    return blobfmt.pack(tensors)
+
+
+def run_denoise(args, rank: int, world: int, local_rank: int):
+    """ltxb_denoise_run over `--denoise-steps` distilled steps and `--blocks`
+    int8 blocks (cycling over `--distinct` uploaded weight sets) at
+    T = 28,160 on the 22x32x40 grid; prints one JSON line with the time per
+    denoising step (max over ranks)."""
+    import ltxb
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    comm = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        uid = [ltxb.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = ltxb.Comm(uid[0], rank, world, local_rank)
+    sets = []
+    for i in range(args.distinct):
+        data, ent = make_blob(dev, seed=i)
+        sets.append(ltxb.build_quant_bufs(ltxb.Blob.from_bytes(data, ent), 0, qset=ltxb.QSET_EXT, hidden=D, ff=FF,
+                                          device=local_rank))
+        del data
+    blocks = [sets[b % len(sets)] for b in range(args.blocks)]
+    cdata, cent = make_core_blob(dev)
+    core = ltxb.Core(ltxb.Blob.from_bytes(cdata, cent), hidden=D, device=local_rank)
+    T = T_TOTAL // world
+    r0 = rank * T
+    g = torch.Generator(device=dev)
+    g.manual_seed(31)
+    clean = torch.randn(T_TOTAL, 128, generator=g, device=dev)[r0:r0 + T].contiguous()
+    noise = torch.randn(T_TOTAL, 128, generator=g, device=dev)[r0:r0 + T].contiguous()
+    ctx = torch.randn(S, D, generator=g, device=dev)
+    mask = torch.ones(T, device=dev)
+    mask_values = torch.ones(1, device=dev)
+    tidx = torch.zeros(T, dtype=torch.int32, device=dev)
+    f, hh, ww = GRID
+    t = torch.arange(r0, r0 + T, device=dev)
+    pos = torch.stack([t // (hh * ww), (t // ww) % hh, t % ww], dim=1).float()
+    cos, sin = ltxb.rope_tables(ltxb.ROPE_AXES, pos, H)
+    sig = ltxb.sched_sigmas(1)[: args.denoise_steps + 1]
+    latent = ltxb.sched_noise_init(clean, noise, mask, 1.0)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    ltxb.denoise(core, blocks, sig[:2], latent.clone(), clean, mask, mask_values, tidx, ctx, cos, sin, comm)  # warm-up
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    ltxb.denoise(core, blocks, sig, latent, clean, mask, mask_values, tidx, ctx, cos, sin, comm)
+    e1.record(stream)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    finite = bool(torch.isfinite(latent).all().item())
+    n = len(sig) - 1
+    if rank == 0:
+        flops = n * (args.blocks * block_flops(T_TOTAL) + 2 * 2.0 * T_TOTAL * D * 128)
+        print(json.dumps({"metric": "denoise_step_ms", "value": round(ms / n, 3), "unit": "ms",
+                          "higher_is_better": False, "n_gpus": world, "denoise_steps": n, "blocks": args.blocks,
+                          "distinct_weight_sets": args.distinct, "tokens": T_TOTAL,
+                          "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "latent_finite": finite,
+                          "api": "ltxb_denoise_run (core parts + blocks + scheduler on the device)"}))
+    for s_ in sets:
+        s_.free()
+    core.free()
+    if comm is not None:
+        comm.free()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -427,6 +519,11 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--denoise", action="store_true",
+                    help="instead of the block metric, time the whole denoising loop (ltxb_denoise_run)")
+    ap.add_argument("--blocks", type=int, default=48, help="--denoise: blocks per step")
+    ap.add_argument("--denoise-steps", type=int, default=8, help="--denoise: distilled steps (<= 8)")
+    ap.add_argument("--distinct", type=int, default=4, help="--denoise: distinct uploaded weight sets")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -437,6 +534,8 @@ def main() -> int:
         raise SystemExit(f"T={T_TOTAL} does not shard over {world} ranks")
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.denoise:
+        return run_denoise(args, rank, world, local_rank)
     return run_ours(args, rank, world, local_rank)
 
 

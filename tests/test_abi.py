@@ -105,3 +105,36 @@ def test_null_arguments_rejected():
     assert ltxb.lib.ltxb_weights_upload(0, None, 0, None, 0, 0, 0, 0, 4096, 16384, ctypes.byref(h)) == ltxb.EINVAL
     ltxb.lib.ltxb_weights_free(None)
     ltxb.lib.ltxb_comm_free(None)
+
+
+def test_blob_writer_matches_reference_packer():
+    """The library's blob writer (ltxb.blobfmt) produces byte-for-byte the
+    format the oracle restates from tools/pack_block.py."""
+    import numpy as np
+    from ltxb import blobfmt
+    from oracle import blob as oblob
+    from oracle import inputs as oin
+    from oracle import ltx_block_ref as ref
+    geom = ref.Geometry(d=256, ff=512)
+    bw = oin.make_weights(geom, 3, quant="int8")
+    tensors = oblob.block_tensors(bw, 2)
+    data_o, ent_o = oblob.pack(tensors)
+    data_l, ent_l = blobfmt.pack(tensors)
+    assert data_o == data_l
+    assert [(e.name, e.offset, e.nbytes, e.sha256) for e in ent_o] == \
+        [(e["name"], e["offset"], e["nbytes"], e["sha256"]) for e in ent_l]
+    names = {e.name[len("transformer_blocks.2."):] for e in ent_o if "::" not in e.name}
+    assert names == {suffix for suffix, _, _ in blobfmt.BLOCK_TENSORS}
+    assert set(blobfmt.Q8_REF) == {oblob.DOTTED[f] for f in ref.Q8_FIELDS}
+    assert set(blobfmt.Q8_EXT) == {oblob.DOTTED[f] for f in ref.Q8_FIELDS_EXT}
+    for suffix, spec, dt in blobfmt.BLOCK_TENSORS:
+        e = next(x for x in ent_o if x.name == "transformer_blocks.2." + suffix)
+        assert list(e.shape) == blobfmt.shape_of(spec, 256, 512) and e.dtype == dt
+
+
+def test_core_tensor_list_matches_oracle():
+    from ltxb import blobfmt
+    from oracle import core_ref as cr
+    got = [(n, blobfmt.shape_of(sp, 512), dt) for n, sp, dt in blobfmt.CORE_TENSORS]
+    want = [(n, list(shape(512)), "F32" if dt == "f32" else "BF16") for n, shape, dt in cr.CORE_SPECS.values()]
+    assert sorted(got) == sorted(want)
