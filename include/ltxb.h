@@ -91,6 +91,14 @@ const char* ltxb_version(void);
  * Synchronises the device. */
 int ltxb_device_status(int clear, uint32_t* site);
 
+/* Failure-detection self-test: one kernel waits, bounded by limit_us
+ * (1 us .. 2 s), on an mbarrier that nothing arrives on -- the path every
+ * kernel's waits take when a producer is lost. Afterwards
+ * ltxb_device_status reports LTXB_ETIMEOUT with site LTXB_SELFTEST_SITE;
+ * the context stays usable once the status is cleared (no fault, no hang). */
+#define LTXB_SELFTEST_SITE 0x7E0
+int ltxb_selftest_wait(uint32_t limit_us, void* stream);
+
 /* ---- measurement -------------------------------------------------------- */
 
 /* Kernels this library has launched in this process (all devices). */

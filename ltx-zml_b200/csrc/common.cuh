@@ -82,9 +82,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 }
 
 // Wait until the phase with the given parity has completed. Returns false
-// (and records a timeout) if that takes longer than kWaitLimitNs, or if another
-// thread of the grid already recorded a failure.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site) {
+// (and records a timeout) if that takes longer than limit_ns (kWaitLimitNs
+// in the kernels), or if another thread of the grid already recorded a
+// failure.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -93,12 +95,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     if (mbar_try_wait(a, parity)) return true;
     if ((++spins & 255u) == 0) {
       if (*(volatile uint32_t*)&g_status != 0u) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         report_timeout(site);
         return false;
       }
     }
   }
+}
+
+// warp_wait with an explicit limit (the device self-test)
+__device__ __forceinline__ bool warp_wait_limit(uint64_t* bar, uint32_t parity, uint32_t site, uint64_t limit_ns) {
+  const bool ok = mbar_wait(bar, parity, site, limit_ns);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // One lane of a fully active warp (elect.sync): warp-uniform roles issue their

@@ -202,6 +202,27 @@ int ltxb_profile_collect(int max_phases, char* names, int name_stride, double* t
   return n;
 }
 
+// One warp waits (bounded, limit_us) on an mbarrier that nothing arrives on:
+// the expiry path every kernel wait takes, exercised without a fault or a
+// hang. Lane 0 of the other warp of the block only initialises the barrier.
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) warp_wait_limit(&bar, 0, LTXB_SELFTEST_SITE, limit_ns);
+}
+
+int ltxb_selftest_wait(uint32_t limit_us, void* stream) {
+  if (limit_us == 0 || limit_us > 2000000) return set_error(LTXB_EINVAL, "self-test wait: limit must be 1 us .. 2 s");
+  selftest_wait_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>((uint64_t)limit_us * 1000);
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "self-test wait");
+}
+
 int ltxb_device_status(int clear, uint32_t* site) {
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return set_cuda_error(e, "cudaDeviceSynchronize");

@@ -60,6 +60,7 @@ def _load() -> ctypes.CDLL:
         "ltxb_last_error": (ctypes.c_char_p, []),
         "ltxb_version": (ctypes.c_char_p, []),
         "ltxb_device_status": (i32, [i32, ctypes.POINTER(ctypes.c_uint32)]),
+        "ltxb_selftest_wait": (i32, [ctypes.c_uint32, vp]),
         "ltxb_launch_count": (u64, []),
         "ltxb_profile_enable": (i32, [i32]),
         "ltxb_profile_collect": (i32, [i32, vp, i32, vp, vp, vp, i32]),
@@ -127,6 +128,21 @@ def device_status(clear: bool = True) -> int:
     """LTXB_OK or LTXB_ETIMEOUT (a bounded device wait expired). Syncs the device."""
     site = ctypes.c_uint32(0)
     return lib.ltxb_device_status(int(clear), ctypes.byref(site))
+
+
+def device_status_site(clear: bool = True) -> tuple[int, int]:
+    """(status, site code of the failing wait)."""
+    site = ctypes.c_uint32(0)
+    rc = lib.ltxb_device_status(int(clear), ctypes.byref(site))
+    return rc, int(site.value)
+
+
+SELFTEST_SITE = 0x7E0
+
+
+def selftest_wait(limit_us: int, stream=None) -> None:
+    """Run the bounded-wait self-test kernel (a wait that nothing satisfies)."""
+    _check(lib.ltxb_selftest_wait(int(limit_us), _stream(stream)))
 
 
 def launch_count() -> int:

@@ -182,3 +182,26 @@ def test_attention_deterministic(cuda):
     b = ltxb.attention(q, k, v)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+def test_bounded_wait_expires_and_context_survives(cuda):
+    """Failure detection without a fault: a kernel waits on an mbarrier that
+    nothing arrives on; the bounded wait expires, the status word reports
+    LTXB_ETIMEOUT with the self-test site, and after clearing it the same
+    context runs kernels normally."""
+    import time
+    import ltxb
+    assert ltxb.device_status() == ltxb.OK
+    t0 = time.perf_counter()
+    ltxb.selftest_wait(50_000)  # 50 ms
+    rc, site = ltxb.device_status_site(clear=True)
+    assert rc == ltxb.ETIMEOUT and site == ltxb.SELFTEST_SITE
+    assert time.perf_counter() - t0 < 5.0
+    assert ltxb.device_status() == ltxb.OK
+    q = torch.randn(256, 2, 128, device=cuda).to(torch.bfloat16)
+    out = ltxb.attention(q, q, q)
+    torch.cuda.synchronize()
+    assert ltxb.device_status() == ltxb.OK
+    assert ref.rel_rms(out.float().cpu(), _attn_ref(q, q, q)) < ATTN_TOL
+    with pytest.raises(ltxb.LtxbError):
+        ltxb.selftest_wait(0)

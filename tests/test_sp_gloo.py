@@ -1,8 +1,14 @@
-"""CPU tests of the sequence-parallel (ring attention) host logic with real
-multi-process ranks over gloo: the library's ring schedule (ltxb_ring_step,
-the same function the block's NCCL ring follows) drives a K/V shard exchange
-between world_size ranks, each rank merges per-shard (m, l, O) online-softmax
-partials, and the result must equal dense attention over all tokens."""
+"""CPU tests of the sequence-parallel host logic with real multi-process ranks
+over gloo:
+
+* the default path: each rank all-gathers the K/V shards, splits the
+  gathered K/V range and merges the per-split (m, l, O) partials the way the
+  combine kernel does; the result must equal dense attention;
+* the ring alternative: the library's ring schedule (ltxb_ring_step, the
+  function the block's NCCL ring follows) drives a K/V shard exchange and
+  each rank merges per-shard partials;
+* a rank that dies before the exchange: the survivor's collective ends with
+  an error within the process group's timeout."""
 
 import math
 import os
@@ -116,3 +122,95 @@ def test_ring_schedule_properties():
                 assert steps[s]["recv"] == ltxb.ring_step(steps[0]["prev"], n, s)["compute"]
     with pytest.raises(ltxb.LtxbError):
         ltxb.ring_step(2, 2, 0)
+
+
+# ---------------------------------------------------------------------------
+# the default sequence-parallel path: K/V all-gather + split-K/V combine
+# ---------------------------------------------------------------------------
+
+def _combine(parts):
+    """The merge of attn_combine_kernel: m = max m_z, weights 2^(m_z - m)."""
+    m = torch.stack([p[0] for p in parts]).amax(0)
+    w = [torch.exp2(p[0] - m) for p in parts]
+    l = sum(wz * p[1] for wz, p in zip(w, parts))
+    o = sum(wz[..., None] * p[2] for wz, p in zip(w, parts))
+    return o / l[..., None]
+
+
+def _allgather_worker(rank, world, port, T, H, splits, seed, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(seed)
+        q_all = torch.randn(world * T, H, 128, generator=g, dtype=torch.float64)
+        k_all = torch.randn(world * T, H, 128, generator=g, dtype=torch.float64)
+        v_all = torch.randn(world * T, H, 128, generator=g, dtype=torch.float64)
+        sl = slice(rank * T, (rank + 1) * T)
+        ks = [torch.empty(T, H, 128, dtype=torch.float64) for _ in range(world)]
+        vs = [torch.empty(T, H, 128, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(ks, k_all[sl].contiguous())
+        dist.all_gather(vs, v_all[sl].contiguous())
+        k, v = torch.cat(ks), torch.cat(vs)
+        n = k.shape[0]
+        bounds = [z * n // splits for z in range(splits + 1)]
+        parts = [_partial(q_all[sl], k[bounds[z]:bounds[z + 1]], v[bounds[z]:bounds[z + 1]]) for z in range(splits)]
+        got = _combine(parts).permute(1, 0, 2)
+        want = ref.sdpa_dense(q_all[sl], k_all, v_all).reshape(T, H, 128)
+        result_q.put((rank, ref.rel_rms(got.numpy(), want.numpy()), torch.equal(k, k_all)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,splits", [(2, 3), (3, 4)])
+def test_allgather_split_attention_gloo(world, splits):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_allgather_worker, args=(r, world, port, 40, 2, splits, 11, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, gathered in res:
+        assert gathered, f"rank {rank}: gathered K differs from the global K"
+        assert err < 1e-12, (rank, err)
+
+
+def _failing_worker(rank, world, port, result_q):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        result_q.put((rank, "raised"))
+        raise SystemExit(3)  # this rank fails before the exchange
+    import time
+    t0 = time.time()
+    try:
+        out = [torch.empty(4) for _ in range(world)]
+        dist.all_gather(out, torch.ones(4))
+        result_q.put((rank, "completed"))
+    except Exception as e:  # the survivor learns of the failure from the collective
+        result_q.put((rank, f"error after {time.time() - t0:.1f}s: {type(e).__name__}"))
+
+
+def test_rank_failure_surfaces_as_an_error_gloo():
+    """A rank that dies before the K/V exchange: the other rank's collective
+    ends with an error within the process group's timeout instead of
+    hanging."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.terminate()
+    assert res[1] == "raised"
+    assert res[0].startswith("error after"), res[0]
