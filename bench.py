@@ -26,6 +26,7 @@ import pathlib
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = pathlib.Path(__file__).resolve().parent
@@ -92,7 +93,10 @@ class ClockSampler:
 
     def __init__(self):
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        # the clock samples go to $LTXB_CLOCKS_DIR (e.g. a folder collected after
+        # the run), else to the system temporary directory
+        out_dir = os.environ.get("LTXB_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = pathlib.Path(out_dir) / f"clocks_{os.getpid()}.csv"
 
     def start(self):
         try:

@@ -65,7 +65,10 @@ def make_tensor(name, shape, dtype, rng):
 
 
 def main() -> int:
-    ref_root = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        print("usage: make_golden.py <checkout of the reference repository>", file=sys.stderr)
+        return 2
+    ref_root = pathlib.Path(sys.argv[1])
     tools = ref_root / "tools"
     rng = np.random.default_rng(20260821)
     with tempfile.TemporaryDirectory() as td:
