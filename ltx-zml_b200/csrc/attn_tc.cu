@@ -24,11 +24,18 @@
 // moves (with an O rescale in TMEM) when the tile max exceeds it by more than
 // 2^8, exp2 split between the MUFU unit and a degree-3 polynomial on the FMA
 // pipe (1 of 8 pairs), row sums in f32; the per-pair arithmetic uses the
-// two-wide f32 instructions (fma/add .f32x2, 3-input max). K/V rows past Tkv are zero-filled by TMA and masked;
-// query rows past Tq are computed and dropped.
+// two-wide f32 instructions (fma/add .f32x2, 3-input max). The two warps of a
+// row exchange their partial maxima once per K/V tile; the first 32 columns
+// of P are computed with the current reference max while that exchange
+// completes (and redone from S in the rare rescale case), then handed to the
+// MMA warp on their own (p_half) so PV starts before the second half is done.
+// K/V rows past Tkv are zero-filled by TMA and masked; query rows past Tq are
+// computed and dropped.
 //
-// Ring attention: with MERGE, the kernel processes one K/V shard and merges
-// its (m, l, O) into an f32 running state instead of writing the output.
+// MERGE: the kernel writes an f32 (m, l, O) state instead of the output --
+// one state per K/V range with split-K/V (grid z = kv_splits), or merged
+// into a running state across the shards of the ring alternative of
+// sequence parallelism; attn_combine_kernel turns the states into the output.
 #define LTXB_LOCAL_STATUS 1  // whole-program device code (no -rdc): own status word
 #include "common.cuh"
 #include "kernels.h"
