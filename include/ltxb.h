@@ -190,7 +190,9 @@ typedef struct {
 
 /* Per-call tensors (device pointers). Shapes for one rank:
  *   x, out   [T, D] f32   (out may alias x)
- *   tstab    [K, 9, D] f32, tidx [T] int32   -- ada rows (ltx/block.zig:47-67)
+ *   tstab    [K, 9, D] f32, tidx [T] int32   -- ada rows (ltx/block.zig:47-67); token t
+ *            reads row tidx[t], or row 0 when tidx[t] is outside [0, K) (the
+ *            reference's select chain)
  *   ctx      [S, D] f32, pts2 [2, D] f32     -- cross-attention K/V modulation
  *   cos, sin [T, H, 64] f32                  -- split-half RoPE tables
  *   workspace: ltxb_block_workspace_bytes(cfg) bytes, 256-byte aligned. */
@@ -326,9 +328,10 @@ int ltxb_core_pts2(const ltxb_core* core, const float* sigma, float* pts2, void*
 /* latent [T, 128] -> x [T, D] (patchify_proj, core_parts.zig:144-146) */
 int ltxb_core_patchify(const ltxb_core* core, const float* latent, int T, float* x, void* stream);
 /* velocity [T, 128] = proj_out(LayerNorm(x) * (1 + sst[1] + e) + sst[0] + e), e the RAW
- * embedded_timestep of each token: emb[tidx[t]] (emb [K, D]), or emb [T, D] per token
- * when tidx is NULL (CoreParts.tailFromEmb, core_parts.zig:148-170) */
-int ltxb_core_tail(const ltxb_core* core, const float* x, const float* emb, const int* tidx, int T, float* velocity,
+ * embedded_timestep of each token: emb[tidx[t]] (emb [K, D]; a tidx outside [0, K)
+ * reads row 0, as the block's table select does), or emb [T, D] per token when tidx
+ * is NULL (K ignored) (CoreParts.tailFromEmb, core_parts.zig:148-170) */
+int ltxb_core_tail(const ltxb_core* core, const float* x, const float* emb, int K, const int* tidx, int T, float* velocity,
                    void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* ---- scheduler: the distilled LTX-2.5 sampler (ltx/scheduler.zig), bit-exact f32 ----

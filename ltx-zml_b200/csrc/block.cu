@@ -154,6 +154,7 @@ struct LinCall {
   const ltxb_weights* w;
   Bufs* b;
   cudaStream_t st;
+  int tk;  // rows of the modulation table (cfg K)
 };
 
 // y = A . L^T with epilogue `epi`; tensor-core modes take bf16 A.
@@ -164,7 +165,7 @@ static int run_lin(const LinCall& lc, const Lin& L, const void* A, int lda, int 
   if (M <= 0) return LTXB_OK;
   if (w->mode == LTXB_MODE_F32)
     return gemm_f32(static_cast<const float*>(A), lda, L.w, M, L.N, L.K, L.b, epi, static_cast<float*>(out), ldo,
-                    ssq, 32, xres, w->sst, tstab, tidx, ada_row, lc.st);
+                    ssq, 32, xres, w->sst, tstab, tidx, lc.tk, ada_row, lc.st);
   GemmArgs g{};
   g.A = A;
   g.lda = lda;
@@ -183,6 +184,7 @@ static int run_lin(const LinCall& lc, const Lin& L, const void* A, int lda, int 
   g.sst = w->sst;
   g.tstab = tstab;
   g.tidx = tidx;
+  g.tk = lc.tk;
   g.ada_row = ada_row;
   g.ada_d = w->D;
   if (L.wq) {
@@ -390,7 +392,7 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   const int T = c->T, S = c->S, D = w->D, FF = w->FF;
   const bool f32 = w->mode == LTXB_MODE_F32;
   const size_t act = f32 ? 4 : 2;
-  LinCall lc{w, &b, st};
+  LinCall lc{w, &b, st, c->K};
   int rc;
 #define CK(x)            \
   do {                   \
@@ -400,10 +402,10 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
 
   // 1. n = modulate(rms(x), ada1, ada0)
   if (stage == LTXB_STAGE_S1_NORM_MSA)
-    return norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, 0, 1, stage_out, 1, nullptr, st);
+    return norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, c->K, 0, 1, stage_out, 1, nullptr, st);
   {
     Phase p("norm_msa", st);
-    CK(norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, 0, 1, b.n, f32, nullptr, st));
+    CK(norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, c->K, 0, 1, b.n, f32, nullptr, st));
   }
   // 2. fused q/k/v projection (+ q/k sums of squares)
   {
@@ -461,7 +463,7 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   // 7. cross-attention query input
   {
     Phase p("norm_ca", st);
-    CK(norm_modulate(b.x_sa, T, D, w->sst, io->tstab, io->tidx, 6, 7, b.n, f32, nullptr, st));
+    CK(norm_modulate(b.x_sa, T, D, w->sst, io->tstab, io->tidx, c->K, 6, 7, b.n, f32, nullptr, st));
   }
   // 8. prompt K/V
   {
@@ -505,10 +507,10 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   }
   // 13. FFN input
   if (stage == LTXB_STAGE_S6_FF_IN)
-    return norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, 3, 4, stage_out, 1, nullptr, st);
+    return norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, c->K, 3, 4, stage_out, 1, nullptr, st);
   {
     Phase p("norm_mlp", st);
-    CK(norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, 3, 4, b.n, f32, nullptr, st));
+    CK(norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, c->K, 3, 4, b.n, f32, nullptr, st));
   }
   // 14. h = gelu(f W1^T)
   {

@@ -48,6 +48,16 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 // ---------------------------------------------------------------------------
 // shared memory / mbarrier
 // ---------------------------------------------------------------------------
+// Row of a per-token modulation table [rows, 9, D] for token t. The reference
+// selects it with a chain (ltx/block.zig:47-67): row 0 by default, replaced by
+// row k where tidx == k for k = 1 .. rows-1. An index outside [0, rows)
+// therefore reads row 0, and no read leaves the table. No tidx: row 0.
+__device__ __forceinline__ int table_row(const int* tidx, int t, int rows) {
+  if (!tidx) return 0;
+  const int k = __ldg(tidx + t);
+  return (unsigned)k < (unsigned)rows ? k : 0;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

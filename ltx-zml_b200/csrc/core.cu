@@ -147,14 +147,17 @@ __global__ void silu_kernel(const float* __restrict__ x, float* __restrict__ y, 
 
 // out = LayerNorm(x) * (1 + fsst[1] + e) + (fsst[0] + e), LayerNorm mean-
 // subtracting with biased variance and eps 1e-6 (ltx/core_parts.zig:30-35,
-// :148-152); e = emb[tidx[t]], or emb[t] without tidx. One CTA per row.
+// :148-152); e = emb[row] with row = tidx[t] chosen as the block's
+// modulation-table row (table_row: out-of-range reads row 0), or emb[t]
+// without tidx. One CTA per row.
 __global__ void __launch_bounds__(256) tail_norm_kernel(const float* __restrict__ x, const float* __restrict__ emb,
-                                                        const int* __restrict__ tidx, const float* __restrict__ fsst,
+                                                        int K, const int* __restrict__ tidx,
+                                                        const float* __restrict__ fsst,
                                                         int D, float* __restrict__ out) {
   __shared__ float red[8];
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * D;
-  const float* er = emb + (size_t)(tidx ? tidx[t] : t) * D;
+  const float* er = emb + (size_t)(tidx ? table_row(tidx, t, K) : t) * D;
   auto block_sum = [&](float v) {
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     __syncthreads();
@@ -332,12 +335,12 @@ static int adaln_mlp(const ltxb_core* c, const Lin& l1, const Lin& l2, const Lin
   float* h = reinterpret_cast<float*>(w + up256((uint64_t)K * 256 * 4));
   float* e2 = reinterpret_cast<float*>(w + up256((uint64_t)K * 256 * 4) + up256((uint64_t)K * D * 4));
   int rc = sinusoid(t, K, sn, st);
-  if (!rc) rc = gemm_f32(sn, 256, l1.w, K, D, 256, l1.b, EPI_F32, h, D, nullptr, 0, nullptr, nullptr, nullptr, nullptr, 0, st);
+  if (!rc) rc = gemm_f32(sn, 256, l1.w, K, D, 256, l1.b, EPI_F32, h, D, nullptr, 0, nullptr, nullptr, nullptr, nullptr, 0, 0, st);
   if (!rc) rc = silu(h, h, (size_t)K * D, st);
   float* e = emb ? emb : e2;
-  if (!rc) rc = gemm_f32(h, D, l2.w, K, D, D, l2.b, EPI_F32, e, D, nullptr, 0, nullptr, nullptr, nullptr, nullptr, 0, st);
+  if (!rc) rc = gemm_f32(h, D, l2.w, K, D, D, l2.b, EPI_F32, e, D, nullptr, 0, nullptr, nullptr, nullptr, nullptr, 0, 0, st);
   if (!rc) rc = silu(e, e2, (size_t)K * D, st);
-  if (!rc) rc = gemm_f32(e2, D, lo.w, K, lo.N, D, lo.b, EPI_F32, out, lo.N, nullptr, 0, nullptr, nullptr, nullptr, nullptr, 0, st);
+  if (!rc) rc = gemm_f32(e2, D, lo.w, K, lo.N, D, lo.b, EPI_F32, out, lo.N, nullptr, 0, nullptr, nullptr, nullptr, nullptr, 0, 0, st);
   return rc;
 }
 
@@ -359,25 +362,26 @@ int ltxb_core_pts2(const ltxb_core* c, const float* sigma, float* pts2, void* wo
 int ltxb_core_patchify(const ltxb_core* c, const float* latent, int T, float* x, void* stream) {
   if (!c || (T > 0 && (!latent || !x))) return set_error(LTXB_EINVAL, "core patchify: null argument");
   return gemm_f32(latent, 128, c->pat.w, T, c->D, 128, c->pat.b, EPI_F32, x, c->D, nullptr, 0, nullptr, nullptr,
-                  nullptr, nullptr, 0, static_cast<cudaStream_t>(stream));
+                  nullptr, nullptr, 0, 0, static_cast<cudaStream_t>(stream));
 }
 
-int ltxb_core_tail(const ltxb_core* c, const float* x, const float* emb, const int* tidx, int T, float* velocity,
+int ltxb_core_tail(const ltxb_core* c, const float* x, const float* emb, int K, const int* tidx, int T, float* velocity,
                    void* workspace, uint64_t workspace_bytes, void* stream) {
   if (!c || (T > 0 && (!x || !emb || !velocity))) return set_error(LTXB_EINVAL, "core tail: null argument");
   if (T <= 0) return LTXB_OK;
+  if (tidx && K <= 0) return set_error(LTXB_EINVAL, "core tail: K must be positive with tidx");
   const uint64_t need = up256((uint64_t)T * c->D * 4);
   if (!workspace || workspace_bytes < need)
     return set_error(LTXB_EINVAL, "core tail: workspace of %llu bytes is smaller than the %llu required",
                      (unsigned long long)workspace_bytes, (unsigned long long)need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* n = static_cast<float*>(workspace);
-  tail_norm_kernel<<<T, 256, 0, st>>>(x, emb, tidx, c->fsst, c->D, n);
+  tail_norm_kernel<<<T, 256, 0, st>>>(x, emb, K, tidx, c->fsst, c->D, n);
   launched();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "tail norm");
   return gemm_f32(n, c->D, c->po.w, T, 128, c->D, c->po.b, EPI_F32, velocity, 128, nullptr, 0, nullptr, nullptr,
-                  nullptr, nullptr, 0, st);
+                  nullptr, nullptr, 0, 0, st);
 }
 
 int ltxb_sched_sigmas(int stage, float* out, int capacity) {
@@ -506,7 +510,7 @@ int ltxb_denoise_run(const ltxb_core* core, const ltxb_weights* const* blocks, i
     if ((rc = ltxb_core_patchify(core, io->latent, T, w.x, st))) return rc;
     for (int b = 0; b < n_blocks; ++b)
       if ((rc = ltxb_block_forward(blocks[b], &bio, cfg, st))) return rc;
-    if ((rc = ltxb_core_tail(core, w.x, w.emb, io->tidx, T, w.vel, w.core, w.core_bytes, st))) return rc;
+    if ((rc = ltxb_core_tail(core, w.x, w.emb, K, io->tidx, T, w.vel, w.core, w.core_bytes, st))) return rc;
     if ((rc = ltxb_sched_step(io->latent, w.vel, w.ts, io->clean, io->mask, T, 128, sigma, sigma_next, io->latent, st)))
       return rc;
   }

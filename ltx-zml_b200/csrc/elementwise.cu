@@ -41,7 +41,7 @@ __device__ __forceinline__ float4 ada4(const float* sst, const float* tstab, int
 __global__ void __launch_bounds__(ROW_THREADS) norm_modulate_kernel(const float* __restrict__ x, int D,
                                                                     const float* __restrict__ sst,
                                                                     const float* __restrict__ tstab,
-                                                                    const int* __restrict__ tidx, int r_shift,
+                                                                    const int* __restrict__ tidx, int tk, int r_shift,
                                                                     int r_scale, void* __restrict__ out, int out_f32,
                                                                     float* __restrict__ rms_copy) {
   __shared__ float red[32];
@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_modulate_kernel(const float*
   }
   ss = block_sum(ss, red);
   const float r = rsqrtf(ss / (float)D + kEps);
-  const int trow = tidx ? tidx[t] : 0;
+  const int trow = table_row(tidx, t, tk);
   for (int i = threadIdx.x; i < nv; i += blockDim.x) {
     const int c = i * 4;
     float4 v = reinterpret_cast<const float4*>(xr)[i];
@@ -87,18 +87,18 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_modulate_kernel(const float*
   }
 }
 
-int norm_modulate(const float* x, int T, int D, const float* sst, const float* tstab, const int* tidx, int r_shift,
+int norm_modulate(const float* x, int T, int D, const float* sst, const float* tstab, const int* tidx, int tk, int r_shift,
                   int r_scale, void* out, int out_f32, float* rms_copy, cudaStream_t st) {
   if (T <= 0) return LTXB_OK;
   if (D % 4) return set_error(LTXB_EINVAL, "norm_modulate: D %% 4");
-  norm_modulate_kernel<<<T, ROW_THREADS, 0, st>>>(x, D, sst, tstab, tidx, r_shift, r_scale, out, out_f32, rms_copy);
+  norm_modulate_kernel<<<T, ROW_THREADS, 0, st>>>(x, D, sst, tstab, tidx, tk, r_shift, r_scale, out, out_f32, rms_copy);
   launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "norm_modulate");
 }
 
 int rms_rows(const float* x, int T, int D, float* out, cudaStream_t st) {
-  return norm_modulate(x, T, D, nullptr, nullptr, nullptr, -1, -1, out, 1, nullptr, st);
+  return norm_modulate(x, T, D, nullptr, nullptr, nullptr, 0, -1, -1, out, 1, nullptr, st);
 }
 
 // q/k norm over the full D from bf16 raw projections and per-N-tile sums of

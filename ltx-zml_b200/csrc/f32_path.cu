@@ -21,7 +21,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
                                                        const __nv_bfloat16* __restrict__ bias, int epi,
                                                        float* __restrict__ out, int ldo, const float* __restrict__ xres,
                                                        const float* __restrict__ sst, const float* __restrict__ tstab,
-                                                       const int* __restrict__ tidx, int ada_row) {
+                                                       const int* __restrict__ tidx, int tk, int ada_row) {
   __shared__ float sa[FB_K][FB_M + 4];
   __shared__ float sw[FB_K][FB_N + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   for (int i = 0; i < 8; ++i) {
     const int gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
     if (gm >= M) continue;
-    const int trow = (epi == EPI_RESID_F32 && tidx) ? tidx[gm] : 0;
+    const int trow = epi == EPI_RESID_F32 ? table_row(tidx, gm, tk) : 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
@@ -88,13 +88,13 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
 
 int gemm_f32(const float* A, int lda, const void* W, int M, int N, int K, const void* bias, int epi, float* out,
              int ldo, float* /*ssq*/, int /*ssq_ld*/, const float* xres, const float* sst, const float* tstab,
-             const int* tidx, int ada_row, cudaStream_t st) {
+             const int* tidx, int tk, int ada_row, cudaStream_t st) {
   if (M <= 0 || N <= 0) return LTXB_OK;
   if (K % FB_K) return set_error(LTXB_EINVAL, "gemm_f32: K %% 16");
   dim3 grid((N + FB_N - 1) / FB_N, (M + FB_M - 1) / FB_M);
   gemm_f32_kernel<<<grid, 256, 0, st>>>(A, lda, reinterpret_cast<const __nv_bfloat16*>(W), M, N, K,
                                         reinterpret_cast<const __nv_bfloat16*>(bias), epi, out, ldo, xres, sst, tstab,
-                                        tidx, ada_row);
+                                        tidx, tk, ada_row);
   launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "gemm_f32");

@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       float ssq = 0.f;
       int trow = 0;
-      if (EPI == EPI_RESID_F32 && row_ok) trow = args.tidx[row];
+      if (EPI == EPI_RESID_F32 && row_ok) trow = table_row(args.tidx, row, args.tk);
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];

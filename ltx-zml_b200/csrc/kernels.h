@@ -69,6 +69,7 @@ struct GemmArgs {
   const float* sst;    // [9, D]
   const float* tstab;  // [K, 9, D]
   const int* tidx;     // [M]
+  int tk;              // rows of tstab
   int ada_row;
   int ada_d;
 };
@@ -113,8 +114,8 @@ int rope_tables(int kind, const float* pos, int T, int H, double theta, float* c
 cudaError_t attn_status(uint32_t* v, bool clear);
 
 // ---- elementwise / normalisation kernels ----
-// n = rms(x) * (1 + ada(r_scale)) + ada(r_shift) -> bf16 or f32 [T, D]
-int norm_modulate(const float* x, int T, int D, const float* sst, const float* tstab, const int* tidx, int r_shift,
+// n = rms(x) * (1 + ada(r_scale)) + ada(r_shift) -> bf16 or f32 [T, D]; tstab has tk rows
+int norm_modulate(const float* x, int T, int D, const float* sst, const float* tstab, const int* tidx, int tk, int r_shift,
                   int r_scale, void* out, int out_f32, float* rms_copy, cudaStream_t st);
 // weightless rms only (s4_normed stage), f32 out
 int rms_rows(const float* x, int T, int D, float* out, cudaStream_t st);
@@ -138,7 +139,7 @@ int qk_norm_rope2(const void* raw_q, const void* raw_k, int ld_raw, const float*
 // C[M, N] = A[M, K] (f32) . W[N, K]^T (bf16 upcast) + bias, epilogues as Epi
 int gemm_f32(const float* A, int lda, const void* W, int M, int N, int K, const void* bias, int epi, float* out,
              int ldo, float* ssq, int ssq_ld, const float* xres, const float* sst, const float* tstab,
-             const int* tidx, int ada_row, cudaStream_t st);
+             const int* tidx, int tk, int ada_row, cudaStream_t st);
 // f32 attention: q/k/v f32 [T, H, 128] (row strides ld*) -> out f32 [Tq, H*128],
 // with optional gate [Tq, ldg]
 int attention_f32(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* out,

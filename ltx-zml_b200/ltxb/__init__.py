@@ -90,7 +90,7 @@ def _load() -> ctypes.CDLL:
         "ltxb_core_adaln": (i32, [vp, vp, i32, vp, vp, vp, u64, vp]),
         "ltxb_core_pts2": (i32, [vp, vp, vp, vp, u64, vp]),
         "ltxb_core_patchify": (i32, [vp, vp, i32, vp, vp]),
-        "ltxb_core_tail": (i32, [vp, vp, vp, vp, i32, vp, vp, u64, vp]),
+        "ltxb_core_tail": (i32, [vp, vp, vp, i32, vp, i32, vp, vp, u64, vp]),
         "ltxb_sched_sigmas": (i32, [i32, vp, i32]),
         "ltxb_denoise_workspace_bytes": (u64, [vp, vp, vp]),
         "ltxb_denoise_run": (i32, [vp, vp, i32, vp, i32, vp, vp, vp]),
@@ -364,11 +364,12 @@ class Core:
         return out
 
     def tail(self, x, emb, tidx=None, stream=None) -> torch.Tensor:
-        """tailFromEmb: x [T, D], emb [K, D] with tidx [T] (or emb [T, D]) -> velocity [T, 128]."""
+        """tailFromEmb: x [T, D], emb [K, D] with tidx [T] (or emb [T, D]) -> velocity [T, 128].
+        A tidx outside [0, K) reads row 0, as the block's table select does."""
         T = x.shape[0]
         out = torch.empty(T, 128, dtype=torch.float32, device=x.device)
         ws = self._ws(T, 1, x.device)
-        _check(lib.ltxb_core_tail(self.handle, _ptr(x), _ptr(emb), _ptr(tidx), T, _ptr(out), _ptr(ws), ws.numel(),
+        _check(lib.ltxb_core_tail(self.handle, _ptr(x), _ptr(emb), emb.shape[0], _ptr(tidx), T, _ptr(out), _ptr(ws), ws.numel(),
                                   _stream(stream)))
         return out
 

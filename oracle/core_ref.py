@@ -223,7 +223,7 @@ def denoise_ref(core: CoreParts, blocks: list, sigmas, latent, clean, mask, mask
         x = core.patchify(c(lat)).to(dtype)
         for b in blocks:
             x = b.block_out(x, ts9, tid, c(ctx), pts2, c(cos), c(sin))
-        vel = core.tail_from_emb(x.double(), emb.double()[tid.long()]).numpy().astype(np.float32)
+        vel = core.tail_from_emb(x.double(), emb.double()[ref.table_index(tid, emb.shape[0])]).numpy().astype(np.float32)
         lat = scheduler_step(lat, vel, ts, clean, mask, sg, sn)
         out.append(lat)
     return out

@@ -80,14 +80,32 @@ def modulate(n: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor) -> torch
     return n * (scale + 1.0) + shift
 
 
+def table_index(tidx: torch.Tensor, rows: int) -> torch.Tensor:
+    """The table row the select chain of ltx/block.zig:58-66 picks for each
+    token: tidx[t] when 0 <= tidx[t] < rows, else row 0."""
+    k = tidx.long()
+    return torch.where((k >= 0) & (k < rows), k, torch.zeros_like(k))
+
+
 def ada_val(table: torch.Tensor, tstab: torch.Tensor, tidx: torch.Tensor, i: int) -> torch.Tensor:
     """ltx/block.zig:47-67: per-token row tstab[tidx[t], i] plus table row i.
 
-    The reference selects rows with a select-chain (bit-exact copy); an index
-    gather is the same selection."""
+    The reference selects rows with a select chain: row 0 everywhere, then
+    row k wherever tidx == k for k = 1 .. K-1 (a bit-exact copy). An index
+    gather with every tidx outside [0, K) sent to row 0 is the same selection
+    (select_chain_rows below restates the chain itself for small K)."""
     chunk = tstab[:, i, :]                    # [K, D]
-    tv = chunk[tidx.long()]                   # [T, D]
+    tv = chunk[table_index(tidx, chunk.shape[0])]   # [T, D]
     return tv + table[i].to(tv.dtype)
+
+
+def select_chain_rows(chunk: torch.Tensor, tidx: torch.Tensor) -> torch.Tensor:
+    """The select chain of ltx/block.zig:58-66 as written: chunk [K, D],
+    tidx [T] -> [T, D]; row 0 by default, row k where tidx == k."""
+    tv = chunk[0:1].expand(tidx.shape[0], -1)
+    for k in range(1, chunk.shape[0]):
+        tv = torch.where((tidx == k)[:, None], chunk[k][None, :], tv)
+    return tv
 
 
 def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:

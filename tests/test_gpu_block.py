@@ -95,6 +95,35 @@ def test_lowp_small_all_stages(cuda, mode):
     assert worst["block_out"] <= max(floor, 1e-4), f"{mode}: {worst['block_out']} worse than torch-bf16 {floor}"
 
 
+@pytest.mark.parametrize("mode", ["f32", "int8"])
+def test_out_of_range_tidx_reads_row0(cuda, mode):
+    """tidx entries outside [0, K) (negative, K, far above) select table row
+    0, as the reference's select chain does (ltx/block.zig:47-67): every
+    stage is bit-identical to the run with those entries set to 0 and matches
+    the oracle's chain semantics. Every consumer of tidx (the norm-modulate
+    rows and the gated-residual epilogues) is covered by the stage list."""
+    import dataclasses
+    import ltxb
+    quant = None if mode == "f32" else "int8"
+    geom, bw, data, ent, qset = helpers.weights_case(SMALL["d"], SMALL["ff"], 2, quant)
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 2, "axes", 3, "random")
+    bad = inp.tidx.copy()
+    bad[::5] = -1
+    bad[1::7] = 3
+    bad[2::11] = 2**31 - 1
+    bad[3::13] = -2**31
+    zeroed = np.where((bad >= 0) & (bad < 3), bad, 0).astype(np.int32)
+    inp_bad = dataclasses.replace(inp, tidx=bad)
+    w = helpers.upload(data, ent, geom, ltxb.MODE_F32 if quant is None else ltxb.MODE_INT8)
+    got = _run_stages(w, helpers.to_cuda(inp_bad, cuda), ref.STAGES)
+    same = _run_stages(w, helpers.to_cuda(dataclasses.replace(inp, tidx=zeroed), cuda), ref.STAGES)
+    for s in ref.STAGES:
+        assert np.array_equal(got[s], same[s]), f"{mode}/{s}: out-of-range tidx differs from row 0"
+    want = helpers.oracle_stages(bw, inp_bad, qset if quant else None)
+    _check(got, want, F32_TOL if quant is None else LOW_TOL, f"{mode}-tidx-oob")
+    w.free()
+
+
 @pytest.mark.parametrize("mode", ["bf16", "int8"])
 def test_lowp_config0(cuda, mode):
     """Config-0 architecture at T = 1024 in bf16 / int8 (config 3's recipe:

@@ -112,6 +112,15 @@ def test_core_adaln_pts2_patchify_tail(cuda, d):
     want_vel = oc.tail_from_emb(torch.from_numpy(xs).double(), emb.cpu().double()[torch.from_numpy(tidx).long()])
     assert ref.rel_rms(vel.cpu().double(), want_vel) < 1e-5
     assert torch.equal(vel, vel_tok)
+    # indices outside [0, K) read row 0, as the block's table select does
+    bad = tidx.copy()
+    bad[::4] = -1
+    bad[1::9] = 3
+    bad[2::10] = 2**31 - 1
+    vel_bad = core.tail(torch.from_numpy(xs).to(cuda), emb, torch.from_numpy(bad).to(cuda))
+    vel_zero = core.tail(torch.from_numpy(xs).to(cuda), emb,
+                         torch.from_numpy(np.where((bad >= 0) & (bad < 3), bad, 0).astype(np.int32)).to(cuda))
+    assert torch.equal(vel_bad, vel_zero)
     core.free()
 
 

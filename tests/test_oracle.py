@@ -190,3 +190,16 @@ def test_ada_gather_matches_select_chain():
     for k in range(1, 3):
         tv = torch.where((tidx == k)[:, None], tstab[k, 4].expand(6, 8), tv)
     assert torch.equal(got, tv + sst[4])
+
+
+def test_ada_out_of_range_tidx_reads_row0():
+    """An index the chain never matches (negative, K or above) keeps the
+    chain's default, row 0, in the gather as in the chain itself."""
+    g = torch.Generator().manual_seed(4)
+    tstab = torch.randn(4, 9, 8, generator=g, dtype=torch.float64)
+    sst = torch.randn(9, 8, generator=g, dtype=torch.float64)
+    tidx = torch.tensor([3, -1, 4, 1, 2**31 - 1, 0, -2**31, 2, 7], dtype=torch.int32)
+    got = ref.ada_val(sst, tstab, tidx, 5)
+    assert torch.equal(got, ref.select_chain_rows(tstab[:, 5], tidx) + sst[5])
+    clamped = torch.where((tidx >= 0) & (tidx < 4), tidx, torch.zeros_like(tidx))
+    assert torch.equal(got, ref.ada_val(sst, tstab, clamped, 5))
