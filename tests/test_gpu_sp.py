@@ -58,11 +58,17 @@ def _worker(rank, world, uid, grid, seed, mode, algo, q):
 
 
 def _run(world, grid, seed, mode, algo="allgather"):
+    return _spawn(world, _worker, (grid, seed, mode, algo))
+
+
+def _spawn(world, target, args):
+    """Runs target(rank, world, uid, *args, q) on `world` spawned ranks and
+    returns the ranks' outputs concatenated along tokens."""
     import ltxb
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     uid = ltxb.Comm.unique_id()
-    procs = [ctx.Process(target=_worker, args=(r, world, uid, grid, seed, mode, algo, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, uid, *args, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -96,4 +102,85 @@ def test_sp_block_matches_single_gpu_and_oracle(mode, grid, algo):
     single = _run(1, grid, seed, mode)
     assert ref.rel_rms(sp, want) < 5e-3
     assert ref.rel_rms(single, want) < 5e-3
+    assert ref.rel_rms(sp, single) < 3e-3
+
+
+def _denoise_case():
+    """Two int8 blocks, the core parts and three distilled steps at D 256 on a
+    2x4x16 grid (128 tokens), a few tokens at mask value 0.5."""
+    from oracle import core_ref as cr
+    import ltxb
+    grid = (2, 4, 16)
+    T = grid[0] * grid[1] * grid[2]
+    inp = helpers.inputs_case(D, grid, S, 4, "axes", 1, "random")
+    rng = np.random.default_rng(9)
+    clean = rng.standard_normal((T, 128)).astype(np.float32)
+    noise = rng.standard_normal((T, 128)).astype(np.float32)
+    mask_values = np.array([1.0, 0.5], dtype=np.float32)
+    tidx = (np.arange(T) % 7 == 0).astype(np.int32)
+    mask = mask_values[tidx]
+    return dict(inp=inp, clean=clean, mask=mask, mask_values=mask_values, tidx=tidx,
+                lat0=cr.noise_init(clean, noise, mask, 1.0), sig=ltxb.sched_sigmas(1)[:4])
+
+
+def _denoise_worker(rank, world, uid, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "ltx-zml_b200"), os.path.join(root, "tests")]
+    import ltxb
+    import helpers as h
+    from oracle import blob as oblob
+    from oracle import core_ref as cr
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        c = _denoise_case()
+        blocks = []
+        for i in range(2):
+            geom, _, data, ent, _ = h.weights_case(D, FF, 20 + i, "int8")
+            blocks.append(h.upload(data, ent, geom, ltxb.MODE_INT8, device=rank))
+        cdata, centries = oblob.pack(cr.core_tensors(cr.make_core_weights(D, 5)))
+        cent = [dict(name=e.name, dtype=e.dtype, shape=e.shape, offset=e.offset, nbytes=e.nbytes) for e in centries]
+        core = ltxb.Core(ltxb.Blob.from_bytes(cdata, cent), hidden=D, device=rank)
+        T = c["lat0"].shape[0] // world
+        sl = slice(rank * T, (rank + 1) * T)
+        g = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        inp = c["inp"]
+        lat = g(c["lat0"][sl])
+        comm = ltxb.Comm(uid, rank, world, rank) if world > 1 else None
+        ltxb.denoise(core, blocks, c["sig"], lat, g(c["clean"][sl]), g(c["mask"][sl]), g(c["mask_values"]),
+                     g(c["tidx"][sl]), g(inp.ctx), g(inp.cos[sl]), g(inp.sin[sl]), comm=comm)
+        torch.cuda.synchronize()
+        q.put((rank, lat.cpu().numpy(), True, ltxb.device_status(), None))
+        if comm is not None:
+            comm.free()
+        core.free()
+        for b in blocks:
+            b.free()
+    except Exception as exc:  # report, never hang the parent
+        q.put((rank, None, False, -99, repr(exc)))
+
+
+def test_sp_denoise_loop_matches_single_gpu_and_oracle():
+    """The whole denoising loop (core parts, two int8 blocks, the scheduler)
+    with tokens split over 2 GPUs: the gathered latent after three steps
+    against the single-GPU loop and the f64 oracle's trajectory (the
+    reference's per-step 2e-3 gate, or the torch-bf16 loop's floor)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from oracle import core_ref as cr
+    sp = _spawn(2, _denoise_worker, ())
+    single = _spawn(1, _denoise_worker, ())
+    c = _denoise_case()
+    inp = c["inp"]
+    bws = [helpers.weights_case(D, FF, 20 + i, "int8")[1::3] for i in range(2)]
+    run = lambda dtype: cr.denoise_ref(cr.CoreParts(cr.make_core_weights(D, 5)),
+                                       [ref.QBlock(bw, dtype, qset=qs) for bw, qs in bws], c["sig"], c["lat0"],
+                                       c["clean"], c["mask"], c["mask_values"], c["tidx"], inp.ctx, inp.cos,
+                                       inp.sin, dtype=dtype)[-1]
+    want = run(torch.float64)
+    tol = max(2e-3, ref.rel_rms(run(torch.bfloat16), want))
+    assert ref.rel_rms(sp, want) <= tol
+    assert ref.rel_rms(single, want) <= tol
     assert ref.rel_rms(sp, single) < 3e-3
