@@ -17,6 +17,9 @@
  *    entry points enqueue work on `stream` and return without a host sync;
  *    device-side failures of bounded waits surface through
  *    ltxb_device_status().
+ *  - Compute entry points run on the calling thread's current device, which
+ *    must be the device a weights / core handle was uploaded to (LTXB_EINVAL
+ *    otherwise, before anything is launched).
  *  - Layouts are row-major. Activations are token-major [T, D] with D = H*128
  *    and heads concatenated (head h occupies columns [128h, 128h+128)).
  *  - Weights are [out, in] row-major as in the checkpoint; int8 weights carry

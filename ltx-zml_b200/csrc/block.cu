@@ -377,6 +377,7 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   if (!w || !io || !c) return set_error(LTXB_EINVAL, "null argument");
   if (c->mode != w->mode) return set_error(LTXB_EINVAL, "config mode %d != weights mode %d", c->mode, w->mode);
   if (c->T <= 0 || c->S <= 0 || c->K <= 0) return set_error(LTXB_EINVAL, "T, S and K must be positive");
+  if (int rc = check_device(w->device, "block")) return rc;
   const bool sp = c->sp_size > 1;
   if (sp && (!c->comm || c->comm->nranks != c->sp_size || c->comm->rank != c->sp_rank))
     return set_error(LTXB_EINVAL, "sp_size > 1 needs a communicator matching sp_rank/sp_size");

@@ -348,6 +348,7 @@ int ltxb_core_adaln(const ltxb_core* c, const float* t, int K, float* emb, float
                     uint64_t workspace_bytes, void* stream) {
   if (!c || !t || !ts9) return set_error(LTXB_EINVAL, "core adaln: null argument");
   if (K <= 0) return LTXB_OK;
+  if (int rc = check_device(c->device, "core adaln")) return rc;
   return adaln_mlp(c, c->ada1, c->ada2, c->ada_out, t, K, emb, ts9, workspace, workspace_bytes,
                    static_cast<cudaStream_t>(stream));
 }
@@ -355,12 +356,15 @@ int ltxb_core_adaln(const ltxb_core* c, const float* t, int K, float* emb, float
 int ltxb_core_pts2(const ltxb_core* c, const float* sigma, float* pts2, void* workspace, uint64_t workspace_bytes,
                    void* stream) {
   if (!c || !sigma || !pts2) return set_error(LTXB_EINVAL, "core pts2: null argument");
+  if (int rc = check_device(c->device, "core pts2")) return rc;
   return adaln_mlp(c, c->pada1, c->pada2, c->pada_out, sigma, 1, nullptr, pts2, workspace, workspace_bytes,
                    static_cast<cudaStream_t>(stream));
 }
 
 int ltxb_core_patchify(const ltxb_core* c, const float* latent, int T, float* x, void* stream) {
   if (!c || (T > 0 && (!latent || !x))) return set_error(LTXB_EINVAL, "core patchify: null argument");
+  if (T > 0)
+    if (int rc = check_device(c->device, "core patchify")) return rc;
   return gemm_f32(latent, 128, c->pat.w, T, c->D, 128, c->pat.b, EPI_F32, x, c->D, nullptr, 0, nullptr, nullptr,
                   nullptr, nullptr, 0, 0, static_cast<cudaStream_t>(stream));
 }
@@ -369,6 +373,7 @@ int ltxb_core_tail(const ltxb_core* c, const float* x, const float* emb, int K, 
                    void* workspace, uint64_t workspace_bytes, void* stream) {
   if (!c || (T > 0 && (!x || !emb || !velocity))) return set_error(LTXB_EINVAL, "core tail: null argument");
   if (T <= 0) return LTXB_OK;
+  if (int rc = check_device(c->device, "core tail")) return rc;
   if (tidx && K <= 0) return set_error(LTXB_EINVAL, "core tail: K must be positive with tidx");
   const uint64_t need = up256((uint64_t)T * c->D * 4);
   if (!workspace || workspace_bytes < need)
@@ -478,6 +483,7 @@ int ltxb_denoise_run(const ltxb_core* core, const ltxb_weights* const* blocks, i
   if (cfg->T <= 0 || cfg->K <= 0 || cfg->S <= 0) return set_error(LTXB_EINVAL, "denoise: T, K and S must be positive");
   for (int b = 0; b < n_blocks; ++b)
     if (!blocks[b]) return set_error(LTXB_EINVAL, "denoise: block %d is null", b);
+  if (int rc = check_device(core->device, "denoise")) return rc;
   const DenoiseWs need = denoise_layout(core, blocks[0], cfg, nullptr);
   if (!io->workspace || io->workspace_bytes < need.total)
     return set_error(LTXB_EINVAL, "denoise: workspace of %llu bytes is smaller than the %llu required",

@@ -13,6 +13,8 @@ namespace ltxb {
 // ---- errors (thread-local message, see ltxb_last_error) ----
 int set_error(int code, const char* fmt, ...);
 int set_cuda_error(cudaError_t e, const char* what);
+// LTXB_EINVAL unless `device` (where a handle's buffers live) is the current device
+int check_device(int device, const char* what);
 int sm_count();
 
 // ---- launch accounting and per-phase profiling ----

@@ -130,6 +130,15 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return LTXB_OK;
 }
 
+int check_device(int device, const char* what) {
+  int cur = -1;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return set_cuda_error(e, what);
+  if (cur != device)
+    return set_error(LTXB_EINVAL, "%s: the weights live on device %d but device %d is current", what, device, cur);
+  return LTXB_OK;
+}
+
 }  // namespace ltxb
 
 using namespace ltxb;
