@@ -198,7 +198,9 @@ typedef struct {
  *            reference's select chain)
  *   ctx      [S, D] f32, pts2 [2, D] f32     -- cross-attention K/V modulation
  *   cos, sin [T, H, 64] f32                  -- split-half RoPE tables
- *   workspace: ltxb_block_workspace_bytes(cfg) bytes, 256-byte aligned. */
+ *   workspace: ltxb_block_workspace_bytes(cfg) bytes, 256-byte aligned.
+ * The f32 tensors must be 16-byte aligned (the kernels move 16-byte vectors)
+ * and tidx 4-byte aligned; a NULL tidx reads row 0 for every token. */
 typedef struct {
   const float* x;
   float* out;
@@ -286,7 +288,11 @@ int ltxb_attention_split(const void* q, const void* k, const void* v, void* out,
  * (ltx/block.zig:462-477). scale_dtype LTXB_DT_F32 or LTXB_DT_BF16.
  * fused != 0 dequantises tiles in shared memory inside the GEMM;
  * fused == 0 expands the weights into `workspace` (N*K*2 bytes) with a
- * bandwidth-bound pass and runs the bf16 GEMM. */
+ * bandwidth-bound pass and runs the bf16 GEMM. Shapes: K a multiple of 128,
+ * N of 128 (fused) or 32. A, Wq, bias, out and workspace 16-byte aligned (TMA and the
+ * epilogue's 16-byte vectors); scales aligned to their element size.
+ * Misaligned pointers or unsupported shapes return LTXB_EINVAL before
+ * anything is launched. */
 int ltxb_dq_gemm(const void* A, const void* Wq, const void* scales, int scale_dtype, const void* bias, void* out,
                  int M, int N, int K, int fused, void* workspace, uint64_t workspace_bytes, void* stream);
 
@@ -401,7 +407,8 @@ int ltxb_dq_gemm_noalloc(const void* A, const void* Wq, const void* scales, int 
                          void* out, int M, int N, int K, void* stream);
 
 /* out[M, N] (bf16) = A[M, K] (bf16) . W[N, K] (bf16)^T (+ bias): the plain
- * bf16 `lin` on tcgen05. */
+ * bf16 `lin` on tcgen05. K a multiple of 64, N of 32; pointers 16-byte
+ * aligned (LTXB_EINVAL otherwise, before anything is launched). */
 int ltxb_gemm_bf16(const void* A, const void* W, const void* bias, void* out, int M, int N, int K, void* stream);
 
 #ifdef __cplusplus

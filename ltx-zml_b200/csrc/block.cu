@@ -377,6 +377,15 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   if (!w || !io || !c) return set_error(LTXB_EINVAL, "null argument");
   if (c->mode != w->mode) return set_error(LTXB_EINVAL, "config mode %d != weights mode %d", c->mode, w->mode);
   if (c->T <= 0 || c->S <= 0 || c->K <= 0) return set_error(LTXB_EINVAL, "T, S and K must be positive");
+  {
+    // the kernels read rows of these tensors as 16-byte vectors
+    const void* v16[] = {io->x, io->out, io->tstab, io->ctx, io->pts2, io->cos, io->sin};
+    for (const void* p : v16)
+      if (!p || (reinterpret_cast<uintptr_t>(p) & 15))
+        return set_error(LTXB_EINVAL, "block io: x, out, tstab, ctx, pts2, cos and sin must be non-null and 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(io->tidx) & 3) return set_error(LTXB_EINVAL, "block io: tidx must be 4-byte aligned");
+    if (reinterpret_cast<uintptr_t>(stage_out) & 15) return set_error(LTXB_EINVAL, "stage_out must be 16-byte aligned");
+  }
   if (int rc = check_device(w->device, "block")) return rc;
   const bool sp = c->sp_size > 1;
   if (sp && (!c->comm || c->comm->nranks != c->sp_size || c->comm->rank != c->sp_rank))

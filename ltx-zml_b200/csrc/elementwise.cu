@@ -327,6 +327,9 @@ __global__ void dequant_weights_kernel(const int8_t* __restrict__ q, const void*
 int dequant_weights(const int8_t* q, const void* scales, int scale_bf16, int N, int K, void* out, cudaStream_t st) {
   if ((size_t)N * K == 0) return LTXB_OK;
   if (K % 128) return set_error(LTXB_EINVAL, "dequant: K %% 128");
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (reinterpret_cast<uintptr_t>(scales) & (scale_bf16 ? 1 : 3)))
+    return set_error(LTXB_EINVAL, "dequant: weights and output must be 16-byte aligned, scales element-aligned");
   const size_t n16 = (size_t)N * K / 16;
   int grid = (int)((n16 + 255) / 256);
   if (grid > 8 * sm_count()) grid = 8 * sm_count();

@@ -364,6 +364,10 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st) {
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15) || (a.lda % 8) ||
       (a.ldb % (a.b_int8 ? 16 : 8)) || (a.ldo % 8))
     return set_error(LTXB_EINVAL, "gemm: operands must be 16-byte aligned with 16-byte row strides");
+  // the epilogue moves 16-byte vectors of out, bias and the residual input
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!a16(a.out) || !a16(a.bias) || !a16(a.xres) || (a.xres && a.ldx % 4))
+    return set_error(LTXB_EINVAL, "gemm: out, bias and residual must be 16-byte aligned");
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda, GEMM_BK, GEMM_BM,
                         CU_TENSOR_MAP_SWIZZLE_128B);

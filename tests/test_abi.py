@@ -138,3 +138,45 @@ def test_core_tensor_list_matches_oracle():
     got = [(n, blobfmt.shape_of(sp, 512), dt) for n, sp, dt in blobfmt.CORE_TENSORS]
     want = [(n, list(shape(512)), "F32" if dt == "f32" else "BF16") for n, shape, dt in cr.CORE_SPECS.values()]
     assert sorted(got) == sorted(want)
+
+
+# Fake device addresses: the operator entry points must reject these
+# arguments on the host, before any CUDA call (none of them is dereferenced).
+_A, _W, _O, _WS, _SC = 0x10000, 0x20000, 0x30000, 0x40000, 0x50000
+
+
+@pytest.mark.parametrize("call,msg", [
+    (lambda l, p: l.ltxb_gemm_bf16(p(_A), p(_W), None, p(_O + 8), 128, 256, 64, None), "16-byte aligned"),
+    (lambda l, p: l.ltxb_gemm_bf16(p(_A), p(_W), p(_SC + 2), p(_O), 128, 256, 64, None), "16-byte aligned"),
+    (lambda l, p: l.ltxb_gemm_bf16(p(_A + 4), p(_W), None, p(_O), 128, 256, 64, None), "16-byte aligned"),
+    (lambda l, p: l.ltxb_gemm_bf16(p(_A), p(_W), None, p(_O), 128, 256, 96, None), "multiple of 64"),
+    (lambda l, p: l.ltxb_gemm_bf16(p(_A), p(_W), None, p(_O), 128, 48, 64, None), "multiple of 32"),
+    (lambda l, p: l.ltxb_gemm_bf16(p(_A), p(_W), None, p(_O), 0, 256, 64, None), "empty shape"),
+    (lambda l, p: l.ltxb_dq_gemm(p(_A), p(_W + 1), p(_SC), 1, None, p(_O), 128, 256, 128, 0, p(_WS), 1 << 20,
+                                 None), "16-byte aligned"),
+    (lambda l, p: l.ltxb_dq_gemm(p(_A), p(_W), p(_SC + 2), 1, None, p(_O), 128, 256, 128, 0, p(_WS), 1 << 20,
+                                 None), "element-aligned"),
+    (lambda l, p: l.ltxb_dq_gemm(p(_A), p(_W), p(_SC), 1, None, p(_O), 128, 256, 128, 0, p(_WS), 1024, None),
+     "workspace"),
+    (lambda l, p: l.ltxb_dq_gemm(p(_A), p(_W), p(_SC), 1, None, p(_O), 128, 256, 64, 1, None, 0, None), "K % 128"),
+    (lambda l, p: l.ltxb_dq_gemm(p(_A), p(_W), p(_SC), 7, None, p(_O), 128, 256, 128, 1, None, 0, None),
+     "scale dtype"),
+    (lambda l, p: l.ltxb_attention(p(_A + 2), p(_W), p(_SC), p(_O), None, 128, 128, 2, ctypes.c_float(0.1), None),
+     "16-byte aligned"),
+    (lambda l, p: l.ltxb_attention(p(_A), p(_W), p(_SC), p(_O), None, 128, 0, 2, ctypes.c_float(0.1), None),
+     "empty K/V"),
+    (lambda l, p: l.ltxb_attention_split(p(_A), p(_W), p(_SC), p(_O), None, 128, 512, 2, ctypes.c_float(0.1), -1,
+                                         p(_WS), 1 << 30, None), "negative split"),
+    (lambda l, p: l.ltxb_attention_split(p(_A), p(_W), p(_SC), p(_O), None, 128, 512, 2, ctypes.c_float(0.1), 2,
+                                         p(_WS), 4096, None), "workspace"),
+    (lambda l, p: l.ltxb_attention_split(p(_A), p(_W), p(_SC), p(_O), None, 128, 512, 2, ctypes.c_float(0.1), 2,
+                                         p(_WS + 16), 1 << 30, None), "256-byte aligned"),
+])
+def test_operator_arguments_rejected_on_the_host(call, msg):
+    """Misaligned operands and unsupported shapes return LTXB_EINVAL with a
+    message before anything reaches the device (a misaligned 16-byte vector
+    access or TMA copy would otherwise fault the GPU)."""
+    import ltxb
+    rc = call(ltxb.lib, ctypes.c_void_p)
+    assert rc == ltxb.EINVAL, (rc, ltxb.last_error())
+    assert msg in ltxb.last_error()
