@@ -59,9 +59,11 @@ extern "C" {
 #define LTXB_MODE_INT8 2  /* reference `QBlock`: int8 g128 q/k/v (x2) + FFN       */
 
 /* Which linears LTXB_MODE_INT8 takes int8 (ltx/loader.zig:147-156 for the
- * reference set; BASELINE config 3 also quantises the output projections). */
-#define LTXB_QSET_REF 0   /* q1,k1,v1,q2,k2,v2,ff1,ff2                           */
+ * reference set; BASELINE config 3 also quantises the output projections;
+ * QBlock.qBlockOut, ltx/block.zig:577-611, keeps the FFN unquantised). */
+#define LTXB_QSET_REF 0   /* q1,k1,v1,q2,k2,v2,ff1,ff2 (qBlockOutAll)            */
 #define LTXB_QSET_EXT 1   /* LTXB_QSET_REF + o1,o2                               */
+#define LTXB_QSET_QKV 2   /* q1,k1,v1,q2,k2,v2; FFN bf16 (qBlockOut)             */
 
 /* Stage selectors for ltxb_block_stage (ltx/block_conformance.zig:311-322). */
 #define LTXB_STAGE_S1_NORM_MSA 0

@@ -590,6 +590,8 @@ int ltxb_weights_upload(int device, const void* blob, uint64_t blob_bytes, const
   *out = nullptr;
   if (!blob || !entries || n_entries <= 0) return set_error(LTXB_EINVAL, "empty blob");
   if (mode < LTXB_MODE_F32 || mode > LTXB_MODE_INT8) return set_error(LTXB_EINVAL, "unknown mode %d", mode);
+  if (mode == LTXB_MODE_INT8 && qset != LTXB_QSET_REF && qset != LTXB_QSET_EXT && qset != LTXB_QSET_QKV)
+    return set_error(LTXB_EINVAL, "unknown quant set %d", qset);
   if (hidden <= 0 || hidden % 256 || ff <= 0 || ff % 256)
     return set_error(LTXB_EINVAL, "hidden (%d) and ff (%d) must be positive multiples of 256", hidden, ff);
   int rc = ltxb_init(device);
@@ -606,6 +608,7 @@ int ltxb_weights_upload(int device, const void* blob, uint64_t blob_bytes, const
   const int D = hidden, H = w->H;
   const bool q8 = mode == LTXB_MODE_INT8;
   const bool qo = q8 && qset == LTXB_QSET_EXT;
+  const bool qf = q8 && qset != LTXB_QSET_QKV;
   rc = u.linear(w->qkv1, {"attn1_to_q", "attn1_to_k", "attn1_to_v"}, D, D, true, q8);
   if (!rc) rc = u.linear(w->g1, {"attn1_to_gate_logits"}, H, D, true, false, w->G - H);
   if (!rc) rc = u.linear(w->o1, {"attn1_to_out_0"}, D, D, true, qo);
@@ -613,8 +616,8 @@ int ltxb_weights_upload(int device, const void* blob, uint64_t blob_bytes, const
   if (!rc) rc = u.linear(w->g2, {"attn2_to_gate_logits"}, H, D, true, false, w->G - H);
   if (!rc) rc = u.linear(w->kv2, {"attn2_to_k", "attn2_to_v"}, D, D, true, q8);
   if (!rc) rc = u.linear(w->o2, {"attn2_to_out_0"}, D, D, true, qo);
-  if (!rc) rc = u.linear(w->ff1, {"ff_net_0_proj"}, ff, D, false, q8);
-  if (!rc) rc = u.linear(w->ff2, {"ff_net_2"}, D, ff, false, q8);
+  if (!rc) rc = u.linear(w->ff1, {"ff_net_0_proj"}, ff, D, false, qf);
+  if (!rc) rc = u.linear(w->ff2, {"ff_net_2"}, D, ff, false, qf);
   if (!rc) rc = u.tensor("attn1_q_norm_weight", LTXB_DT_BF16, D, 0, &w->qn1);
   if (!rc) rc = u.tensor("attn1_k_norm_weight", LTXB_DT_BF16, D, 0, &w->kn1);
   if (!rc) rc = u.tensor("attn2_q_norm_weight", LTXB_DT_BF16, D, 0, &w->qn2);

@@ -9,7 +9,9 @@ sm_100a library:
   Blob.open / check_layout / find_entry      ltx/loader.zig:45-129
   build_block_bufs / build_quant_bufs        ltx/loader.zig:133-172
   Block.s1NormMsa ... blockOut, wBlockOut     ltx/block.zig:248-353
-  QBlock.qBlockOutAll                        ltx/block.zig:544-574
+  Block.wAttn1                               ltx/block.zig:274-276
+  QBlock.qBlockOutAll / qBlockOut            ltx/block.zig:544-611
+  Chain.chainB23 / chainB47 / wChainB47      ltx/block.zig:434-455
   attention (whileSdpa / sdpa)               ltx/block.zig:105-154, :234
   dq_gemm (linQ)                             ltx/block.zig:462-477
 
@@ -36,7 +38,7 @@ OK = 0
 EINVAL, ECUDA, ENOMEM, ELAYOUT, EMISSING, EDTYPE, ENCCL, ETIMEOUT, EUNSUPPORTED = range(-1, -10, -1)
 DT_BF16, DT_F32, DT_I8 = 0, 1, 2
 MODE_F32, MODE_BF16, MODE_INT8 = 0, 1, 2
-QSET_REF, QSET_EXT = 0, 1
+QSET_REF, QSET_EXT, QSET_QKV = 0, 1, 2
 STAGES = ["s1_norm_msa", "s1b_qnorm", "s2_attn1_nogate", "s3_attn1", "s4_after_sa", "s4_normed",
           "s5_ca_out", "s6_ff_in", "s7_ff_out", "block_out"]
 _DT = {"BF16": DT_BF16, "F32": DT_F32, "I8": DT_I8}
@@ -256,9 +258,10 @@ class Blob:
 class Weights:
     """Device-resident weights of one block (an `ltxb_weights*`)."""
 
-    def __init__(self, handle, mode, hidden, ff, device):
+    def __init__(self, handle, mode, hidden, ff, device, qset=QSET_REF):
         self.handle = handle
         self.mode = mode
+        self.qset = qset
         self.D = hidden
         self.FF = ff
         self.H = hidden // 128
@@ -286,7 +289,7 @@ def _upload(blob: Blob, block_idx: int, mode: int, qset: int, hidden: int, ff: i
     h = ctypes.c_void_p()
     _check(lib.ltxb_weights_upload(device, host.ctypes.data, host.size, ctypes.addressof(arr), len(arr),
                                    block_idx, mode, qset, hidden, ff, ctypes.byref(h)))
-    return Weights(h, mode, hidden, ff, device)
+    return Weights(h, mode, hidden, ff, device, qset)
 
 
 def build_block_bufs(blob: Blob, block_idx: int, mode: int = MODE_BF16, hidden: int = 4096, ff: int = 16384,
@@ -297,7 +300,9 @@ def build_block_bufs(blob: Blob, block_idx: int, mode: int = MODE_BF16, hidden: 
 
 def build_quant_bufs(blob: Blob, block_idx: int, qset: int = QSET_REF, hidden: int = 4096, ff: int = 16384,
                      device: int = 0) -> Weights:
-    """ltx/loader.zig:158-172: int8 g128 pairs for the quantised linears."""
+    """ltx/loader.zig:158-172: int8 g128 pairs for the quantised linears
+    (QSET_REF: qBlockOutAll's set; QSET_EXT: + output projections; QSET_QKV:
+    q/k/v only, qBlockOut's set)."""
     return _upload(blob, block_idx, MODE_INT8, qset, hidden, ff, device)
 
 
@@ -547,6 +552,12 @@ class Block:
         online softmax, which the reference gates against dense at 1e-5."""
         return self.forward(x, tstab, tidx, ctx, pts2, cos, sin)
 
+    def wAttn1(self, x, tstab, tidx, cos, sin, ctx=None, pts2=None):
+        """ltx/block.zig:274-276: s3Attn1 with the blockwise softmax -- the
+        same call as s3Attn1 here. The stage reads neither ctx nor pts2; rows
+        of x stand in for them unless given."""
+        return self.s3Attn1(x, tstab, tidx, x[:1] if ctx is None else ctx, x[:2] if pts2 is None else pts2, cos, sin)
+
     def s1NormMsa(self, *a):
         return self.stage("s1_norm_msa", *a)
 
@@ -615,11 +626,46 @@ class HostPipe:
 
 
 class QBlock(Block):
-    """ltx/block.zig:481-574: the block with int8 g128 linears."""
+    """ltx/block.zig:481-611: the block with int8 g128 linears. Which linears
+    are int8 is fixed when the weights are uploaded (the quant set)."""
 
     def qBlockOutAll(self, x, tstab, tidx, ctx, pts2, cos, sin):
-        assert self.w.mode == MODE_INT8
+        """ltx/block.zig:544-574: int8 q/k/v of both attentions and the FFN
+        (weights uploaded with QSET_REF, or QSET_EXT which adds the output
+        projections)."""
+        if self.w.mode != MODE_INT8 or self.w.qset not in (QSET_REF, QSET_EXT):
+            raise LtxbError(EINVAL, "qBlockOutAll needs int8 weights uploaded with QSET_REF or QSET_EXT")
         return self.forward(x, tstab, tidx, ctx, pts2, cos, sin)
+
+    def qBlockOut(self, x, tstab, tidx, ctx, pts2, cos, sin):
+        """ltx/block.zig:577-611: int8 q/k/v of both attentions, the FFN
+        unquantised (weights uploaded with QSET_QKV)."""
+        if self.w.mode != MODE_INT8 or self.w.qset != QSET_QKV:
+            raise LtxbError(EINVAL, "qBlockOut needs int8 weights uploaded with QSET_QKV")
+        return self.forward(x, tstab, tidx, ctx, pts2, cos, sin)
+
+
+class Chain:
+    """ltx/block.zig:434-455: three blocks (the harness's b0, b23, b47) run
+    back to back on the same conditioning."""
+
+    def __init__(self, b0: Block, b23: Block, b47: Block):
+        self.b0, self.b23, self.b47 = b0, b23, b47
+
+    def chainB23(self, x, tstab, tidx, ctx, pts2, cos, sin):
+        y = self.b0.blockOut(x, tstab, tidx, ctx, pts2, cos, sin)
+        return self.b23.blockOut(y, tstab, tidx, ctx, pts2, cos, sin)
+
+    def chainB47(self, x, tstab, tidx, ctx, pts2, cos, sin):
+        y = self.chainB23(x, tstab, tidx, ctx, pts2, cos, sin)
+        return self.b47.blockOut(y, tstab, tidx, ctx, pts2, cos, sin)
+
+    def wChainB47(self, x, tstab, tidx, ctx, pts2, cos, sin):
+        """The same chain through wBlockOut (one function here: attention is
+        always blockwise)."""
+        y = self.b0.wBlockOut(x, tstab, tidx, ctx, pts2, cos, sin)
+        y = self.b23.wBlockOut(y, tstab, tidx, ctx, pts2, cos, sin)
+        return self.b47.wBlockOut(y, tstab, tidx, ctx, pts2, cos, sin)
 
 
 # ---------------------------------------------------------------------------

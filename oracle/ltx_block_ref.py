@@ -202,6 +202,9 @@ F32_FIELDS = ("sst", "psst")
 Q8_FIELDS = ("q1_w", "k1_w", "v1_w", "q2_w", "k2_w", "v2_w", "ff1_w", "ff2_w")
 # BASELINE's extension: output projections quantised too.
 Q8_FIELDS_EXT = Q8_FIELDS + ("o1_w", "o2_w")
+# QBlock.qBlockOut's set (ltx/block.zig:577-611): q/k/v of both attentions,
+# the FFN left unquantised.
+Q8_FIELDS_QKV = ("q1_w", "k1_w", "v1_w", "q2_w", "k2_w", "v2_w")
 
 
 @dataclass
@@ -337,6 +340,19 @@ class Block:
     def s3_attn1(self, x, tstab, tidx, cos, sin):
         return self.attn1_out(x, tstab, tidx, cos, sin, "dense")
 
+    def w_attn1(self, x, tstab, tidx, cos, sin):
+        """ltx/block.zig:274-276: attn1 with the blockwise online softmax."""
+        return self.attn1_out(x, tstab, tidx, cos, sin, "blockwise")
+
+    def f_logits(self, x, tstab, tidx, cos, sin):
+        """ltx/block.zig:356-365: self-attention's pre-softmax logits q.k over
+        hd (no 1/sqrt(hd) scale), after q/k norm and RoPE -> [Tq, H, Tk]."""
+        n = self.s1_norm_msa(x, tstab, tidx)
+        q = rope(rms_w(lin(n, self.w["q1_w"], self.w["q1_b"]), self.w["qn1"]), cos, sin)
+        k = rope(rms_w(lin(n, self.w["k1_w"], self.w["k1_b"]), self.w["kn1"]), cos, sin)
+        t = q.shape[0]
+        return torch.einsum("qhd,khd->qhk", q.reshape(t, self.h, HD), k.reshape(t, self.h, HD))
+
     def after_sa(self, x, tstab, tidx, cos, sin, algo="dense"):
         gate = ada_val(self.w["sst"], tstab, tidx, 2)
         return x + self.attn1_out(x, tstab, tidx, cos, sin, algo) * gate
@@ -434,6 +450,42 @@ class QBlock(Block):
 
     def q_block_out_all(self, *a):
         return self.block_out(*a)
+
+
+# The reference's quantisation probes (ltx/block_conformance.zig:488-494):
+# (Block method, QBlock method, the weights QBlock's method quantises, budget
+# of rel-RMS(q, f)). QBlock's probe methods quantise only the linears they
+# name (ltx/block.zig:513-611): qLogits q1/k1 (:513-517), qAttn1 q1/k1/v1
+# (:520-530), qBlockOut q/k/v of both attentions (:577-611), qFfOut the FFN
+# applied to the unquantised block's s6FfIn (:539-541), qBlockOutAll the
+# reference int8 set (:544-574). With QBlock = the block on dequantised
+# weights, each probe is the Block method on that field set.
+QUANT_PROBES = [
+    ("f_logits", ("q1_w", "k1_w"), 5e-2),
+    ("s3_attn1", ("q1_w", "k1_w", "v1_w"), 2e-2),
+    ("block_out", Q8_FIELDS_QKV, 2e-2),
+    ("s7_ff_out", ("ff1_w", "ff2_w"), 5e-2),
+    ("block_out", Q8_FIELDS, 2e-2),
+]
+PROBE_NAMES = {"f_logits": ("fLogits", "qLogits"), "s3_attn1": ("s3Attn1", "qAttn1"),
+               "s7_ff_out": ("s7FfOut", "qFfOut")}
+
+
+def quant_probes(w: BlockWeights, x, tstab, tidx, ctx, pts2, cos, sin, dtype=torch.float64) -> list:
+    """The probe table above on one input: [(f name, q name, rel-RMS, budget)]."""
+    base = Block(w, dtype)
+    out = []
+    for meth, fields, budget in QUANT_PROBES:
+        qb = QBlock(w, dtype, qset=fields)
+        if meth in ("f_logits", "s3_attn1"):
+            args = (x, tstab, tidx, cos, sin)
+        else:
+            args = (x, tstab, tidx, ctx, pts2, cos, sin)
+        f = getattr(base, meth)(*args)
+        q = getattr(qb, meth)(*args)
+        fn, qn = PROBE_NAMES.get(meth, ("blockOut", "qBlockOutAll" if fields == Q8_FIELDS else "qBlockOut"))
+        out.append((fn, qn, rel_rms(q, f), budget))
+    return out
 
 
 def rel_rms(got, want) -> float:

@@ -95,6 +95,60 @@ def test_lowp_small_all_stages(cuda, mode):
     assert worst["block_out"] <= max(floor, 1e-4), f"{mode}: {worst['block_out']} worse than torch-bf16 {floor}"
 
 
+def test_qblockout_qkv_set(cuda):
+    """QBlock.qBlockOut (ltx/block.zig:577-611): int8 q/k/v of both
+    attentions with the FFN unquantised (QSET_QKV). Every stage within the
+    low-precision bar of the oracle on the same dequantised q/k/v and no
+    worse than torch-bf16; qBlockOut is the block call; a handle of the
+    wrong set refuses the other method."""
+    import ltxb
+    geom, bw, data, ent, _ = helpers.weights_case(SMALL["d"], SMALL["ff"], 1, "int8")
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 1, "axes", 3, "random")
+    want = helpers.oracle_stages(bw, inp, ref.Q8_FIELDS_QKV)
+    w = ltxb.build_quant_bufs(ltxb.Blob.from_bytes(data, ent), 0, qset=ltxb.QSET_QKV, hidden=geom.d, ff=geom.ff)
+    got = _run_stages(w, helpers.to_cuda(inp, cuda), ref.STAGES)
+    worst = _check(got, want, LOW_TOL, "int8-qkv")
+    floor = _bf16_floor(bw, inp, ref.Q8_FIELDS_QKV)
+    assert worst["block_out"] <= max(floor, 1e-4), f"{worst['block_out']} worse than torch-bf16 {floor}"
+    q = ltxb.QBlock(w)
+    out = q.qBlockOut(*helpers.to_cuda(inp, cuda))
+    assert np.array_equal(out.double().cpu().numpy(), got["block_out"])
+    with pytest.raises(ltxb.LtxbError):
+        q.qBlockOutAll(*helpers.to_cuda(inp, cuda))
+    w.free()
+
+
+def test_chain_and_wattn1(cuda):
+    """Chain (ltx/block.zig:434-455): three f32-mode blocks back to back,
+    against the oracle's chain at the f32 bar, and bit-identical to the
+    blockOut calls composed by hand; wChainB47 is the same function here.
+    wAttn1 (ltx/block.zig:274-276) is s3Attn1's call."""
+    import ltxb
+    cases = [helpers.weights_case(SMALL["d"], SMALL["ff"], 30 + i, None) for i in range(3)]
+    inp = helpers.inputs_case(SMALL["d"], SMALL["grid"], SMALL["s"], 3, "axes", 3, "random")
+    ws = [helpers.upload(data, ent, geom, ltxb.MODE_F32) for geom, _, data, ent, _ in cases]
+    blocks = [ltxb.Block(w) for w in ws]
+    chain = ltxb.Chain(*blocks)
+    a = helpers.to_cuda(inp, cuda)
+    c23 = chain.chainB23(*a)
+    c47 = chain.chainB47(*a)
+    w47 = chain.wChainB47(*a)
+    by_hand = blocks[2].blockOut(blocks[1].blockOut(blocks[0].blockOut(*a), *a[1:]), *a[1:])
+    torch.cuda.synchronize()
+    assert torch.equal(c47, by_hand) and torch.equal(w47, c47)
+    t = inp.torch()
+    ob = [ref.Block(bw) for _, bw, _, _, _ in cases]
+    y23 = ob[1].block_out(ob[0].block_out(*t), *t[1:])
+    y47 = ob[2].block_out(y23, *t[1:])
+    assert ref.rel_rms(c23.double().cpu().numpy(), y23) <= F32_TOL
+    assert ref.rel_rms(c47.double().cpu().numpy(), y47) <= F32_TOL
+    x, tstab, tidx, ctx, pts2, cos, sin = a
+    assert torch.equal(blocks[0].wAttn1(x, tstab, tidx, cos, sin), blocks[0].s3Attn1(*a))
+    assert ltxb.device_status() == ltxb.OK
+    for w in ws:
+        w.free()
+
+
 @pytest.mark.parametrize("mode", ["f32", "int8"])
 def test_out_of_range_tidx_reads_row0(cuda, mode):
     """tidx entries outside [0, K) (negative, K, far above) select table row

@@ -203,3 +203,42 @@ def test_ada_out_of_range_tidx_reads_row0():
     assert torch.equal(got, ref.select_chain_rows(tstab[:, 5], tidx) + sst[5])
     clamped = torch.where((tidx >= 0) & (tidx < 4), tidx, torch.zeros_like(tidx))
     assert torch.equal(got, ref.ada_val(sst, tstab, clamped, 5))
+
+
+def test_quant_probes_within_reference_budgets():
+    """The reference's five quantisation probes (ltx/block_conformance.zig:
+    488-494: qLogits 5e-2, qAttn1 2e-2, qBlockOut 2e-2, qFfOut 5e-2,
+    qBlockOutAll 2e-2 against the unquantised block) on the oracle, int8 g128
+    weights without outlier channels. Each probe must show a nonzero error
+    (its linears really are quantised) inside its budget."""
+    geom = ref.Geometry(d=256, ff=512)
+    bw = oin.make_weights(geom, 0, quant="int8", outliers=False)
+    inp = oin.make_inputs(geom, grid=(2, 4, 8), s=16, seed=0)
+    probes = ref.quant_probes(bw, *inp.torch())
+    assert [(f, q) for f, q, _, _ in probes] == [("fLogits", "qLogits"), ("s3Attn1", "qAttn1"),
+                                                 ("blockOut", "qBlockOut"), ("s7FfOut", "qFfOut"),
+                                                 ("blockOut", "qBlockOutAll")]
+    for f, q, err, budget in probes:
+        assert 0 < err < budget, (f, q, err, budget)
+
+
+def test_logits_and_blockwise_attn1():
+    """fLogits is q.k before the softmax: softmax(logits / sqrt(hd)) applied
+    to v reproduces s2Attn1NoGate's attention core; wAttn1 (blockwise
+    softmax) equals s3Attn1 (dense) to rounding (ltx/block_conformance.zig:
+    391-406 gates them at 1e-5)."""
+    geom = ref.Geometry(d=256, ff=512)
+    bw = oin.make_weights(geom, 1)
+    inp = oin.make_inputs(geom, grid=(2, 4, 8), s=16, seed=1)
+    x, tstab, tidx, ctx, pts2, cos, sin = inp.torch()
+    blk = ref.Block(bw)
+    lg = blk.f_logits(x, tstab, tidx, cos, sin)
+    t, h = x.shape[0], geom.h
+    assert lg.shape == (t, h, t)
+    n = blk.s1_norm_msa(x, tstab, tidx)
+    v = ref.lin(n, blk.w["v1_w"], blk.w["v1_b"]).reshape(t, h, ref.HD)
+    p = torch.softmax(lg / np.sqrt(ref.HD), dim=2)
+    core = torch.einsum("qhk,khd->qhd", p, v).reshape(t, h * ref.HD)
+    want = ref.lin(core, blk.w["o1_w"], blk.w["o1_b"])
+    assert ref.rel_rms(want, blk.s2_attn1_nogate(x, tstab, tidx, cos, sin)) < 1e-12
+    assert ref.rel_rms(blk.w_attn1(x, tstab, tidx, cos, sin), blk.s3_attn1(x, tstab, tidx, cos, sin)) < 1e-12
