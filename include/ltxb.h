@@ -144,6 +144,36 @@ typedef struct ltxb_weights ltxb_weights;
  * Returns LTXB_ELAYOUT with the reference's error name in the message. */
 int ltxb_blob_check_layout(const ltxb_entry* entries, int n_entries, uint64_t blob_bytes, uint32_t align);
 
+/* ---- native blob reader (tools/pack_block.py's format) ----
+ * ltxb_blob_open reads <dir>/blob_manifest.json and maps <dir>/blob.bin
+ * read-only, as Blob.open does (ltx/loader.zig:50-69): blob.bin's size must
+ * equal total_bytes (ELAYOUT "BlobSizeMismatch"), the layout must pass
+ * ltxb_blob_check_layout, and `verify` selects SHA-256 checks: the whole
+ * blob against blob_sha256 (the loader's first-touch check,
+ * ltx/loader.zig:270-276) and/or every entry against its own digest (ELAYOUT
+ * "BlobDigestMismatch"). Missing files: EMISSING. Entry dtypes other than
+ * BF16 / F32 / I8 read as -1; shape[] holds the first two dimensions. */
+typedef struct ltxb_blob ltxb_blob;
+#define LTXB_VERIFY_BLOB 1
+#define LTXB_VERIFY_ENTRIES 2
+int ltxb_blob_open(const char* dir, int verify, ltxb_blob** out);
+void ltxb_blob_close(ltxb_blob* blob);
+/* The mapped bytes and the manifest's entries, valid until ltxb_blob_close:
+ * what ltxb_weights_upload / ltxb_core_upload take. Any output may be NULL. */
+int ltxb_blob_view(const ltxb_blob* blob, const void** data, uint64_t* bytes, const ltxb_entry** entries,
+                   int* n_entries, uint32_t* align, int64_t* block);
+/* findEntry (ltx/loader.zig:122-129): the entry whose normalised name
+ * ('.' and '::' -> '_') is `name`; EMISSING otherwise. */
+int ltxb_blob_find(const ltxb_blob* blob, const char* name, const ltxb_entry** out);
+/* The digest checks of ltxb_blob_open on an open blob. */
+int ltxb_blob_verify(const ltxb_blob* blob, int verify);
+/* SHA-256 (FIPS 180-4) of a host buffer: 64 lowercase hex digits + NUL. */
+void ltxb_sha256_hex(const void* data, uint64_t bytes, char hex[65]);
+/* Which SHA-256 code runs: portable_only != 0 forces the portable C++ path;
+ * 0 uses the x86 SHA extensions when the CPU has them. Returns 1 when the
+ * extensions are in use. For tests that compare the two. */
+int ltxb_sha256_impl(int portable_only);
+
 /* Upload one block's weights from a host blob into device-resident buffers
  * on `device` (replaces buildBlockBufs + buildQuantBufs, ltx/loader.zig:
  * 133-172). mode LTXB_MODE_F32/BF16 uploads the 28 base tensors; mode

@@ -23,9 +23,7 @@ is no fallback.
 from __future__ import annotations
 
 import ctypes
-import hashlib
 import json
-import mmap
 import pathlib
 
 import numpy as np
@@ -39,6 +37,7 @@ EINVAL, ECUDA, ENOMEM, ELAYOUT, EMISSING, EDTYPE, ENCCL, ETIMEOUT, EUNSUPPORTED 
 DT_BF16, DT_F32, DT_I8 = 0, 1, 2
 MODE_F32, MODE_BF16, MODE_INT8 = 0, 1, 2
 QSET_REF, QSET_EXT, QSET_QKV = 0, 1, 2
+VERIFY_BLOB, VERIFY_ENTRIES = 1, 2
 STAGES = ["s1_norm_msa", "s1b_qnorm", "s2_attn1_nogate", "s3_attn1", "s4_after_sa", "s4_normed",
           "s5_ca_out", "s6_ff_in", "s7_ff_out", "block_out"]
 _DT = {"BF16": DT_BF16, "F32": DT_F32, "I8": DT_I8}
@@ -67,6 +66,14 @@ def _load() -> ctypes.CDLL:
         "ltxb_profile_enable": (i32, [i32]),
         "ltxb_profile_collect": (i32, [i32, vp, i32, vp, vp, vp, i32]),
         "ltxb_blob_check_layout": (i32, [vp, i32, u64, ctypes.c_uint32]),
+        "ltxb_blob_open": (i32, [ctypes.c_char_p, i32, ctypes.POINTER(vp)]),
+        "ltxb_blob_close": (None, [vp]),
+        "ltxb_blob_view": (i32, [vp, ctypes.POINTER(vp), ctypes.POINTER(u64), ctypes.POINTER(vp),
+                                 ctypes.POINTER(i32), ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int64)]),
+        "ltxb_blob_find": (i32, [vp, ctypes.c_char_p, ctypes.POINTER(vp)]),
+        "ltxb_blob_verify": (i32, [vp, i32]),
+        "ltxb_sha256_hex": (None, [vp, u64, ctypes.c_char_p]),
+        "ltxb_sha256_impl": (i32, [i32]),
         "ltxb_weights_upload": (i32, [i32, vp, u64, vp, i32, i32, i32, i32, i32, i32, ctypes.POINTER(vp)]),
         "ltxb_weights_bytes": (u64, [vp]),
         "ltxb_weights_free": (None, [vp]),
@@ -215,27 +222,61 @@ def normalize_name(name: str) -> str:
     return name.replace("::", "_").replace(".", "_")
 
 
-class Blob:
-    """A packed block (blob.bin + blob_manifest.json, tools/pack_block.py),
-    memory-mapped like ltx/loader.zig:50-69."""
+class _BlobMapping:
+    """Owns an ltxb_blob handle. The Blob and every view of its bytes hold a
+    reference, so the mapping is released only when the last of them goes."""
 
-    def __init__(self, data, manifest: dict):
+    def __init__(self, handle):
+        self.handle = handle
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib.ltxb_blob_close(self.handle)
+                self.handle = None
+        except Exception:
+            pass
+
+
+class Blob:
+    """A packed block (blob.bin + blob_manifest.json, tools/pack_block.py).
+    `Blob.open` goes through the library's native reader (ltxb_blob_open:
+    manifest parse, size and layout checks, read-only mapping, SHA-256),
+    like ltx/loader.zig:50-82; `data` is a uint8 view of the mapping."""
+
+    def __init__(self, data, manifest: dict, mapping: _BlobMapping | None = None):
         self.data = data
         self.manifest = manifest
+        self._map = mapping
 
     @classmethod
-    def open(cls, directory, verify_digest: bool = False) -> "Blob":
-        d = pathlib.Path(directory)
-        man = json.loads((d / "blob_manifest.json").read_text())
-        path = d / "blob.bin"
-        if path.stat().st_size != man["total_bytes"]:
-            raise LtxbError(ELAYOUT, "BlobSizeMismatch")
-        with open(path, "rb") as f:
-            data = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) if man["total_bytes"] else b""
-        blob = cls(data, man)
-        if verify_digest and hashlib.sha256(data).hexdigest() != man["blob_sha256"]:
-            raise LtxbError(ELAYOUT, "BlobDigestMismatch")
-        return blob
+    def open(cls, directory, verify_digest: bool = False, verify_entries: bool = False) -> "Blob":
+        """verify_digest: the whole blob against blob_sha256 (the loader's
+        first-touch check, ltx/loader.zig:270-276); verify_entries: every
+        entry against its own digest (parallel over host cores)."""
+        h = ctypes.c_void_p()
+        flags = (VERIFY_BLOB if verify_digest else 0) | (VERIFY_ENTRIES if verify_entries else 0)
+        _check(lib.ltxb_blob_open(str(directory).encode(), flags, ctypes.byref(h)))
+        mapping = _BlobMapping(h)
+        p, nbytes = ctypes.c_void_p(), ctypes.c_uint64()
+        _check(lib.ltxb_blob_view(h, ctypes.byref(p), ctypes.byref(nbytes), None, None, None, None))
+        n = int(nbytes.value)
+        if n:
+            buf = (ctypes.c_uint8 * n).from_address(p.value)
+            buf._owner = mapping  # views of the bytes keep the mapping alive
+            data = np.ctypeslib.as_array(buf)
+        else:
+            data = np.zeros(0, np.uint8)
+        # the manifest's metadata (names, shapes, digests, provenance); the
+        # native reader has checked the same file
+        man = json.loads((pathlib.Path(directory) / "blob_manifest.json").read_text())
+        return cls(data, man, mapping)
+
+    def verify(self, entries: bool = False) -> None:
+        """The digest checks of `open` on demand (ltxb_blob_verify)."""
+        if self._map is None:
+            raise LtxbError(EINVAL, "verify needs a blob from Blob.open")
+        _check(lib.ltxb_blob_verify(self._map.handle, VERIFY_BLOB | (VERIFY_ENTRIES if entries else 0)))
 
     @classmethod
     def from_bytes(cls, data: bytes, entries: list[dict], align: int = 64, block: int = 0) -> "Blob":

@@ -1,9 +1,10 @@
 /* A plain-C host of libltxb.so: what a Zig (or any C-ABI) caller sees. It
  * exercises the host-side entry points that need no GPU -- the blob layout
- * check with the loader's error cases, the ring schedule, the scheduler's
- * sigma lists, error reporting -- and prints one line per check for the
- * pytest driver (tests/test_c_host.py), which compiles it with gcc against
- * include/ltxb.h. Exit status 0 when every check passes. */
+ * check with the loader's error cases, the native blob reader on a packed
+ * blob directory given as the first argument, the ring schedule, the
+ * scheduler's sigma lists, error reporting -- and prints one line per check
+ * for the pytest driver (tests/test_c_host.py), which compiles it with gcc
+ * against include/ltxb.h. Exit status 0 when every check passes. */
 #include <stdio.h>
 #include <string.h>
 
@@ -16,8 +17,40 @@ static void check(int ok, const char* what) {
   if (!ok) ++failures;
 }
 
-int main(void) {
+/* Blob.open + checkLayout + findEntry + the digest check (ltx/loader.zig:
+ * 50-129, :270-276) through the native reader */
+static void blob_checks(const char* dir) {
+  ltxb_blob* b = NULL;
+  check(ltxb_blob_open(dir, LTXB_VERIFY_BLOB | LTXB_VERIFY_ENTRIES, &b) == LTXB_OK && b != NULL,
+        "blob: open with both digest checks");
+  if (!b) return;
+  const void* data = NULL;
+  uint64_t bytes = 0;
+  const ltxb_entry* ents = NULL;
+  int n = 0;
+  uint32_t align = 0;
+  int64_t block = -1;
+  check(ltxb_blob_view(b, &data, &bytes, &ents, &n, &align, &block) == LTXB_OK && data && bytes > 0 && n > 0 &&
+            align == 64 && block == 0,
+        "blob: view");
+  check(ltxb_blob_check_layout(ents, n, bytes, align) == LTXB_OK, "blob: entries pass the layout check");
+  const ltxb_entry* e = NULL;
+  check(ltxb_blob_find(b, "transformer_blocks_0_attn1_to_q_weight_q8", &e) == LTXB_OK && e &&
+            e->dtype == LTXB_DT_I8 && e->ndim == 2 && e->offset + e->nbytes <= bytes,
+        "blob: findEntry");
+  check(ltxb_blob_find(b, "transformer_blocks_0_missing", &e) == LTXB_EMISSING &&
+            strstr(ltxb_last_error(), "no entry named") != NULL,
+        "blob: MissingEntry");
+  char hex[65];
+  ltxb_sha256_hex("abc", 3, hex);
+  check(strlen(hex) == 64, "sha256 hex digest");
+  ltxb_blob_close(b);
+  check(ltxb_blob_open("/nonexistent-blob-dir", 0, &b) == LTXB_EMISSING && b == NULL, "blob: missing directory");
+}
+
+int main(int argc, char** argv) {
   check(ltxb_version() != NULL && strlen(ltxb_version()) > 0, "version string");
+  if (argc > 1) blob_checks(argv[1]);
 
   /* blob layout (ltx/loader.zig:73-82): 64-byte aligned, no gap, no tail */
   ltxb_entry e[2];

@@ -180,3 +180,152 @@ def test_operator_arguments_rejected_on_the_host(call, msg):
     rc = call(ltxb.lib, ctypes.c_void_p)
     assert rc == ltxb.EINVAL, (rc, ltxb.last_error())
     assert msg in ltxb.last_error()
+
+
+# ---- the native blob reader (ltxb_blob_*) and its SHA-256 ----
+
+def _sha_hex(lib, data: bytes) -> str:
+    out = ctypes.create_string_buffer(65)
+    buf = ctypes.create_string_buffer(data, len(data)) if data else None
+    lib.ltxb_sha256_hex(buf, len(data), out)
+    return out.value.decode()
+
+
+@pytest.mark.parametrize("portable", [1, 0])
+def test_sha256_matches_hashlib(portable):
+    """FIPS 180-4 SHA-256 of the library against hashlib: every length 0..300
+    (all padding cases) and a few large buffers, for the portable code and
+    (where the CPU has them) the x86 SHA extensions."""
+    import hashlib
+    import os
+
+    import ltxb
+    lib = ltxb.lib
+    try:
+        lib.ltxb_sha256_impl(portable)
+        for n in list(range(0, 301)) + [4096, 65537, 1 << 20]:
+            data = os.urandom(n)
+            assert _sha_hex(lib, data) == hashlib.sha256(data).hexdigest(), n
+    finally:
+        lib.ltxb_sha256_impl(0)
+
+
+def _view(lib, h):
+    p, nb, ent, n = ctypes.c_void_p(), ctypes.c_uint64(), ctypes.c_void_p(), ctypes.c_int()
+    al, blk = ctypes.c_uint32(), ctypes.c_int64()
+    assert lib.ltxb_blob_view(h, ctypes.byref(p), ctypes.byref(nb), ctypes.byref(ent), ctypes.byref(n),
+                              ctypes.byref(al), ctypes.byref(blk)) == 0
+    import ltxb
+    arr = (ltxb._Entry * n.value).from_address(ent.value) if n.value else []
+    return p.value, nb.value, list(arr), al.value, blk.value
+
+
+def test_native_blob_open_matches_manifest():
+    """ltxb_blob_open on the reference packer's output: both digest checks
+    pass, the mapped bytes are blob.bin, every entry equals the manifest's
+    (name, dtype, shape, offset, nbytes), and findEntry works."""
+    import ltxb
+    lib = ltxb.lib
+    h = ctypes.c_void_p()
+    assert lib.ltxb_blob_open(str(GOLD).encode(), ltxb.VERIFY_BLOB | ltxb.VERIFY_ENTRIES, ctypes.byref(h)) == 0, \
+        ltxb.last_error()
+    try:
+        p, nb, ents, al, blk = _view(lib, h)
+        raw = (GOLD / "blob.bin").read_bytes()
+        assert nb == len(raw) and ctypes.string_at(p, nb) == raw
+        man = json.loads((GOLD / "blob_manifest.json").read_text())
+        assert al == man["align"] and blk == man["block"] and len(ents) == len(man["entries"])
+        for e, m in zip(ents, man["entries"]):
+            assert e.name.decode() == m["name"]
+            assert e.dtype == {"BF16": 0, "F32": 1, "I8": 2}[m["dtype"]]
+            assert e.ndim == len(m["shape"]) and list(e.shape)[:e.ndim] == m["shape"]
+            assert (e.offset, e.nbytes) == (m["offset"], m["nbytes"])
+        out = ctypes.c_void_p()
+        assert lib.ltxb_blob_find(h, b"transformer_blocks_0_attn1_to_q_weight_q8scale", ctypes.byref(out)) == 0
+        found = ltxb._Entry.from_address(out.value)
+        assert found.name.decode() == "transformer_blocks.0.attn1.to_q.weight::q8scale" and found.dtype == 1
+        assert lib.ltxb_blob_find(h, b"transformer_blocks_0_nope", ctypes.byref(out)) == ltxb.EMISSING
+        assert lib.ltxb_blob_verify(h, ltxb.VERIFY_BLOB | ltxb.VERIFY_ENTRIES) == 0
+    finally:
+        lib.ltxb_blob_close(h)
+
+
+def _blob_dir(tmp_path, data: bytes, manifest_text: str):
+    (tmp_path / "blob.bin").write_bytes(data)
+    (tmp_path / "blob_manifest.json").write_text(manifest_text)
+    return str(tmp_path).encode()
+
+
+def _open_rc(d, flags=0):
+    import ltxb
+    h = ctypes.c_void_p()
+    rc = ltxb.lib.ltxb_blob_open(d, flags, ctypes.byref(h))
+    if rc == 0:
+        ltxb.lib.ltxb_blob_close(h)
+    return rc, ltxb.last_error()
+
+
+def test_native_blob_errors(tmp_path):
+    """The loader's error cases through the native reader: missing files,
+    size and digest mismatches (whole blob and one entry), layout errors and
+    malformed manifests."""
+    import ltxb
+    raw = (GOLD / "blob.bin").read_bytes()
+    mtext = (GOLD / "blob_manifest.json").read_text()
+    man = json.loads(mtext)
+    assert _open_rc(str(tmp_path / "none").encode())[0] == ltxb.EMISSING
+    rc, msg = _open_rc(_blob_dir(tmp_path, raw[:-1], mtext))
+    assert rc == ltxb.ELAYOUT and "BlobSizeMismatch" in msg
+    bad = bytearray(raw)
+    e3 = man["entries"][3]
+    bad[e3["offset"] + 5] ^= 0x40
+    d = _blob_dir(tmp_path, bytes(bad), mtext)
+    assert _open_rc(d)[0] == 0  # no digest asked for
+    rc, msg = _open_rc(d, ltxb.VERIFY_BLOB)
+    assert rc == ltxb.ELAYOUT and "BlobDigestMismatch" in msg
+    rc, msg = _open_rc(d, ltxb.VERIFY_ENTRIES)
+    assert rc == ltxb.ELAYOUT and "BlobDigestMismatch" in msg and e3["name"] in msg
+    m2 = json.loads(mtext)
+    m2["entries"][1]["offset"] += 4
+    rc, msg = _open_rc(_blob_dir(tmp_path, raw, json.dumps(m2)))
+    assert rc == ltxb.ELAYOUT and "Misaligned" in msg
+    for text, what in [(mtext[:-20], "truncated"), ("[]", "not an object"),
+                       (json.dumps({k: v for k, v in man.items() if k != "total_bytes"}), "total_bytes"),
+                       (json.dumps(dict(man, entries={})), "entries"),
+                       ("[" * 100 + "]" * 100, "nesting")]:
+        rc, msg = _open_rc(_blob_dir(tmp_path, raw, text))
+        assert rc == ltxb.ELAYOUT and "manifest" in msg, (what, rc, msg)
+    assert ltxb.lib.ltxb_blob_open(b"x", 4, ctypes.byref(ctypes.c_void_p())) == ltxb.EINVAL
+
+
+def test_native_manifest_parser_details(tmp_path):
+    """JSON the reference's parser accepts: escapes and non-ASCII in names,
+    unknown fields (any type, nested, exponent numbers) ignored, other dtypes
+    read as -1."""
+    import ltxb
+    data = bytes(range(64)) + bytes(8)
+    man = {"packer_version": 1, "x": {"nested": [1, 2.5e3, None, True, {"y": "z"}]}, "align": 64,
+           "block": -7, "total_bytes": 72, "blob_sha256": "",
+           "entries": [{"name": "a.b\"c\\u00e9\U0001F600", "dtype": "BF16", "shape": [32], "offset": 0,
+                        "nbytes": 64, "sha256": "", "extra": [[]]},
+                       {"name": "tail", "dtype": "F16", "shape": [2, 2], "offset": 64, "nbytes": 8}]}
+    d = _blob_dir(tmp_path, data, json.dumps(man, ensure_ascii=True))
+    h = ctypes.c_void_p()
+    assert ltxb.lib.ltxb_blob_open(d, 0, ctypes.byref(h)) == 0, ltxb.last_error()
+    try:
+        _, nb, ents, al, blk = _view(ltxb.lib, h)
+        assert (nb, al, blk) == (72, 64, -7)
+        assert ents[0].name.decode("utf-8") == man["entries"][0]["name"]
+        assert ents[1].dtype == -1 and ents[1].ndim == 2 and list(ents[1].shape) == [2, 2]
+    finally:
+        ltxb.lib.ltxb_blob_close(h)
+
+
+def test_blob_view_outlives_the_blob_object():
+    """Blob.open's bytes stay mapped while any view of them is alive."""
+    import gc
+
+    import ltxb
+    data = ltxb.Blob.open(GOLD, verify_digest=True, verify_entries=True).data
+    gc.collect()
+    assert bytes(data[:4096]) == (GOLD / "blob.bin").read_bytes()[:4096]

@@ -1,7 +1,8 @@
 """The C ABI from plain C (no Python, no torch): tests/c_host/abi_host.c is
 compiled with gcc against include/ltxb.h, linked to libltxb.so, and run. It
 covers the host-side entry points a Zig or C caller uses before any GPU
-work (blob layout check, ring schedule, sigma lists, error reporting)."""
+work (blob layout check, the native blob reader on the reference packer's
+output, ring schedule, sigma lists, error reporting)."""
 
 import pathlib
 import shutil
@@ -21,9 +22,10 @@ def test_c_host_program(tmp_path):
     subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", str(ROOT / "include"),
                     str(ROOT / "tests" / "c_host" / "abi_host.c"), "-L", str(LIB_DIR), "-lltxb",
                     "-Wl,-rpath," + str(LIB_DIR), "-o", str(exe)], check=True)
-    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    r = subprocess.run([str(exe), str(ROOT / "tests" / "golden" / "ref_tools")], capture_output=True, text=True,
+                       timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
-    assert "0 failure(s)" in r.stdout
+    assert "0 failure(s)" in r.stdout and "ok blob: open with both digest checks" in r.stdout
 
 
 @pytest.mark.gpu
