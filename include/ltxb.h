@@ -201,7 +201,17 @@ int ltxb_comm_id_bytes(void);
 int ltxb_comm_get_id(void* id);
 /* Every rank: join the group (NCCL over NVLink; one rank per GPU). */
 int ltxb_comm_init(const void* id, int rank, int nranks, int device, ltxb_comm** out);
+/* Waits for the communicator's queued transfers, then frees it. */
 void ltxb_comm_free(ltxb_comm* c);
+/* The error NCCL has recorded on the communicator, if any
+ * (ncclCommGetAsyncError): LTXB_OK or LTXB_ENCCL with NCCL's message. A host
+ * watchdog polls it while block calls are in flight. */
+int ltxb_comm_check(ltxb_comm* c);
+/* Frees the communicator without waiting (ncclCommAbort): for a host that
+ * knows a peer rank is gone. Collectives in flight on it end without
+ * completing; the block calls that used it must be treated as failed and
+ * their outputs discarded. */
+void ltxb_comm_abort(ltxb_comm* c);
 
 /* Ring schedule of the sequence-parallel self-attention (host-side, no GPU):
  * at step s (0 <= s < nranks) rank r computes against K/V shard

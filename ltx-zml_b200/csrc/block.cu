@@ -819,6 +819,26 @@ void ltxb_comm_free(ltxb_comm* c) {
   delete c;
 }
 
+int ltxb_comm_check(ltxb_comm* c) {
+  if (!c || !c->nccl) return set_error(LTXB_EINVAL, "comm check: null communicator");
+  ncclResult_t async = ncclSuccess;
+  ncclResult_t r = ncclCommGetAsyncError(c->nccl, &async);
+  if (r != ncclSuccess) return set_error(LTXB_ENCCL, "ncclCommGetAsyncError: %s", ncclGetErrorString(r));
+  if (async != ncclSuccess && async != ncclInProgress)
+    return set_error(LTXB_ENCCL, "communicator error: %s", ncclGetErrorString(async));
+  return LTXB_OK;
+}
+
+void ltxb_comm_abort(ltxb_comm* c) {
+  if (!c) return;
+  // abort first: it ends the NCCL kernels still waiting for peers, so the
+  // streams and events below no longer depend on a rank that is gone
+  if (c->nccl) ncclCommAbort(c->nccl);
+  for (auto& e : c->ev) cudaEventDestroy(e);
+  if (c->comm_stream) cudaStreamDestroy(c->comm_stream);  // releases once its work has ended
+  delete c;
+}
+
 // ---- standalone operators ----
 int ltxb_attention(const void* q, const void* k, const void* v, void* out, const float* gate, int Tq, int Tkv, int H,
                    float scale, void* stream) {

@@ -81,6 +81,8 @@ def _load() -> ctypes.CDLL:
         "ltxb_comm_get_id": (i32, [vp]),
         "ltxb_comm_init": (i32, [vp, i32, i32, i32, ctypes.POINTER(vp)]),
         "ltxb_comm_free": (None, [vp]),
+        "ltxb_comm_check": (i32, [vp]),
+        "ltxb_comm_abort": (None, [vp]),
         "ltxb_block_workspace_bytes": (u64, [vp, vp]),
         "ltxb_ring_step": (i32, [i32, i32, i32, vp, vp, vp, vp]),
         "ltxb_block_forward": (i32, [vp, vp, vp, vp]),
@@ -482,6 +484,16 @@ class Comm:
     def free(self):
         if self.handle:
             lib.ltxb_comm_free(self.handle)
+            self.handle = None
+
+    def check(self) -> None:
+        """Raises LtxbError(ENCCL) if NCCL has recorded an error on the group."""
+        _check(lib.ltxb_comm_check(self.handle))
+
+    def abort(self):
+        """Frees the group without waiting for its transfers (a peer is gone)."""
+        if self.handle:
+            lib.ltxb_comm_abort(self.handle)
             self.handle = None
 
 

@@ -49,6 +49,8 @@ def _worker(rank, world, uid, grid, seed, mode, algo, q):
         out2 = blk.forward(*part)  # second call reuses the ring buffers
         torch.cuda.synchronize()
         st = ltxb.device_status()
+        if comm is not None:
+            comm.check()  # no error recorded on the group
         q.put((rank, out.cpu().numpy(), bool(torch.equal(out, out2)), st, None))
         if comm is not None:
             comm.free()
