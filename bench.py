@@ -3,7 +3,8 @@
 (22x32x40 latent grid, D 4096, 32x128 heads, FFN 16384,
 128 text tokens, int8 grouped-128 weights with bf16 scales for the q/k/v,
 output and FFN projections), on 1..N B200s of one node with the tokens
-sharded across ranks (sequence-parallel ring attention over NVLink).
+sharded across ranks (sequence-parallel self-attention: a head-group
+pipelined K/V all-gather over NVLink, NCCL).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -380,13 +381,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 if top in tj:
                     roofline["traffic"] = tj[top]["bytes_per_launch"]
             roofline["peak_source"] = pk["source"] + " (MEASURED_PEAKS.json; sustained for a kernel inside a long step)"
+        sp_algo = ("send/recv ring" if os.environ.get("LTXB_SP_RING") == "1"
+                   else "head-group pipelined K/V all-gather")
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "int8 DiT block, T=28160 (22x32x40), D=4096, 32x128 heads, S=128, FF=16384",
                        "weights": "int8 g128 (bf16 scales) q/k/v/o x2 + FFN; bf16 gates/norms/biases",
-                       "parallelism": f"sp{world} (ring attention over NVLink)" if world > 1 else "single GPU",
+                       "parallelism": (f"sp{world} ({sp_algo} over NVLink)" if world > 1 else "single GPU"),
                        "tokens_per_rank": T, "l2": "inputs larger than L2 (x 461 MB f32, weights 0.7 GB)"},
             "frac_of_peak": round(value / world / pk["bf16"], 4),
             "frac_of_sustained_peak": round(value / world / pk["bf16_sustained"], 4),
