@@ -11,16 +11,21 @@ traced block, `ltx/block.zig`, op for op:
   lin              ltx/block.zig:22-26    y = x . W^T (+ b), W upcast from bf16
   rms_no_w/rms_w   ltx/block.zig:28-34    x * rsqrt(mean(x^2) + 1e-6) (* w)
   modulate         ltx/block.zig:36-38    n * (1 + scale) + shift
-  ada_val          ltx/block.zig:47-67    sst[i] + tstab[tidx[t], i]
+  ada_val          ltx/block.zig:47-67    sst[i] + tstab[tidx[t], i] (row 0 for
+                                          tidx outside [0, K): the select chain)
   rope             ltx/block.zig:71-77    split-half rotation, pairs (i, i+64)
   while_sdpa       ltx/block.zig:105-154  online softmax over K/V chunks,
                                           1/sqrt(hd) applied to K, m0 = -FLT_MAX
   sdpa_dense       zml.nn.sdpa as used at ltx/block.zig:234,525,563
   Block.attention  ltx/block.zig:212-244  qk-norm over full D, RoPE, SDPA,
                                           2*sigmoid per-head gate, out-proj
-  Block stages     ltx/block.zig:248-353  s1 ... s7, block_out, w_block_out
+  Block stages     ltx/block.zig:248-353  s1 ... s7, block_out, w_block_out,
+                                          w_attn1, f_logits
   dq / lin_q       ltx/block.zig:462-477  int8 grouped-128 dequant linear
-  QBlock           ltx/block.zig:481-574  q_block_out_all (q/k/v x2 + FFN int8)
+  QBlock           ltx/block.zig:481-611  the block on dequantised weights of a
+                                          field set: q_block_out_all (q/k/v x2 +
+                                          FFN), qBlockOut (q/k/v x2), the probes
+  quant_probes     ltx/block_conformance.zig:488-494  the five quant budgets
 
 Parity status: the block arithmetic is **parity unpinned** against reference
 artifacts. The reference is Zig on ZML/XLA (no zig/bazel here) and its own f64
