@@ -212,10 +212,12 @@ def make_inputs(device, rank: int, world: int, seed: int = 0):
 # CPU baseline: the oracle's block in torch f32 on the host cores
 # ---------------------------------------------------------------------------
 
-def cpu_block_sample(steps: int, warmup: int):
+def cpu_block_sample(steps: int, warmup: int, budget_s: float = 1e9):
     """Times the CPU restatement (oracle.ltx_block_ref.QBlock, torch f32, all
     host threads) on the config-0 token count, same architecture and int8
-    weights. Returns (TFLOP/s, ms per sample block, threads)."""
+    weights: `warmup` untimed blocks, then `steps` timed ones, stopping early
+    once `budget_s` seconds have been timed. Returns (TFLOP/s, ms per sample
+    block, threads, blocks timed)."""
     from oracle import inputs as oin
     from oracle import ltx_block_ref as ref
     torch.set_num_threads(os.cpu_count() or 1)
@@ -228,21 +230,27 @@ def cpu_block_sample(steps: int, warmup: int):
         for _ in range(warmup):
             blk.w_block_out(*args)
         t0 = time.perf_counter()
-        for _ in range(steps):
+        done = 0
+        while done < steps:
             blk.w_block_out(*args)
-        dt = (time.perf_counter() - t0) / max(1, steps)
-    return block_flops(CPU_SAMPLE_T) / dt / 1e12, dt * 1e3, torch.get_num_threads()
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        dt = (time.perf_counter() - t0) / max(1, done)
+    return block_flops(CPU_SAMPLE_T) / dt / 1e12, dt * 1e3, torch.get_num_threads(), done
 
 
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return 0
     steps, warm = max(1, args.steps), max(0, args.warmup)
-    # bounded sample: at most 3 timed CPU blocks (each ~1-3 s)
-    tflops, ms, cores = cpu_block_sample(min(steps, 3), min(warm, 1))
+    # each step is one block on a bounded sample (T = 1024, ~0.3-1 s on the
+    # host); the timed steps stop after 120 s so the run ends within minutes
+    tflops, ms, cores, timed = cpu_block_sample(steps, min(warm, 3), budget_s=120.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tflops, 4), "unit": "TFLOP/s", "n_gpus": world,
-        "steps": steps, "warmup": warm, "ms_per_step": round(block_flops(T_TOTAL) / (tflops * 1e12) * 1e3, 1),
+        "steps": timed, "steps_requested": steps, "warmup": min(warm, 3),
+        "ms_per_step": round(block_flops(T_TOTAL) / (tflops * 1e12) * 1e3, 1),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "int8 DiT block, T=28160 (22x32x40), D=4096, S=128, FF=16384",
                    "sample": f"CPU restatement at T={CPU_SAMPLE_T}; ms_per_step extrapolated at the sample's TFLOP/s"},
@@ -407,10 +415,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         }
         if world == 1 and not args.no_cpu:
             try:
-                tf, cms, cores = cpu_block_sample(1, 1)
+                # ~10 s of timed CPU work: repeated blocks at the config-0 token count
+                tf, cms, cores, nb = cpu_block_sample(100, 1, budget_s=10.0)
                 line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
                                         "sample": f"oracle QBlock, torch f32 on {cores} host threads, T={CPU_SAMPLE_T}"
-                                                  f" (config-0 shape), {cms:.0f} ms per block"}
+                                                  f" (config-0 shape), {nb} blocks, {cms:.0f} ms per block"}
             except Exception as exc:  # the baseline is reported, never required
                 line["cpu_baseline"] = {"value": None, "error": repr(exc)[:200]}
         print(json.dumps(line), flush=True)
