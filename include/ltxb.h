@@ -174,6 +174,39 @@ void ltxb_sha256_hex(const void* data, uint64_t bytes, char hex[65]);
  * extensions are in use. For tests that compare the two. */
 int ltxb_sha256_impl(int portable_only);
 
+/* ---- streaming staging of blobs (ltx/loader.zig:176-321) ----
+ * Two host slots (page-locked when pinned != 0, so device copies from them
+ * run at the link's full rate) and a reader thread: for schedule position
+ * pos = 0, 1, ... the thread waits for a free slot, checks the blob's digest
+ * on its first touch (verify != 0), and copies blobs[schedule[pos]] into the
+ * slot while the caller uploads from the other one. The caller takes the
+ * positions in order: ltxb_stage_acquire (bounded by timeout_ms:
+ * LTXB_ETIMEOUT), upload, ltxb_stage_release -- or ltxb_stage_upload, which
+ * does the three for a block's weights. Slots move free -> filling -> ready
+ * -> in_use -> free; any other move is LTXB_EINVAL. Checked before any I/O:
+ * every schedule entry names a blob ("ScheduleOutOfRange") and fits a slot
+ * ("SlotTooSmall"). A reader failure (e.g. "BlobDigestMismatch") is returned
+ * by every acquire of a position not staged before it; after
+ * ltxb_stage_abort acquire returns "RingShutdown". The blobs must stay open
+ * while the stage exists. */
+typedef struct ltxb_stage ltxb_stage;
+typedef struct {
+  uint64_t reader_parks;    /* reader waits for a free slot   */
+  uint64_t consumer_parks;  /* acquire waits for a ready slot */
+  uint64_t copy_ns;         /* reader time copying into slots */
+  uint64_t verify_ns;       /* reader time hashing blobs      */
+  uint64_t staged_bytes;
+} ltxb_stage_stats;
+int ltxb_stage_create(const ltxb_blob* const* blobs, int n_blobs, const int* schedule, int n_schedule,
+                      uint64_t slot_bytes, int pinned, int verify, ltxb_stage** out);
+int ltxb_stage_acquire(ltxb_stage* stage, int pos, const void** data, uint64_t* bytes, uint32_t timeout_ms);
+int ltxb_stage_release(ltxb_stage* stage, int pos);
+int ltxb_stage_upload(ltxb_stage* stage, int pos, int device, int block_idx, int mode, int qset, int hidden, int ff,
+                      uint32_t timeout_ms, ltxb_weights** out);
+int ltxb_stage_get_stats(ltxb_stage* stage, ltxb_stage_stats* out);
+void ltxb_stage_abort(ltxb_stage* stage);
+void ltxb_stage_free(ltxb_stage* stage);
+
 /* Upload one block's weights from a host blob into device-resident buffers
  * on `device` (replaces buildBlockBufs + buildQuantBufs, ltx/loader.zig:
  * 133-172). mode LTXB_MODE_F32/BF16 uploads the 28 base tensors; mode

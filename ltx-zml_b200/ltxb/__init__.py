@@ -74,6 +74,13 @@ def _load() -> ctypes.CDLL:
         "ltxb_blob_verify": (i32, [vp, i32]),
         "ltxb_sha256_hex": (None, [vp, u64, ctypes.c_char_p]),
         "ltxb_sha256_impl": (i32, [i32]),
+        "ltxb_stage_create": (i32, [vp, i32, vp, i32, u64, i32, i32, ctypes.POINTER(vp)]),
+        "ltxb_stage_acquire": (i32, [vp, i32, ctypes.POINTER(vp), ctypes.POINTER(u64), ctypes.c_uint32]),
+        "ltxb_stage_release": (i32, [vp, i32]),
+        "ltxb_stage_upload": (i32, [vp, i32, i32, i32, i32, i32, i32, i32, ctypes.c_uint32, ctypes.POINTER(vp)]),
+        "ltxb_stage_get_stats": (i32, [vp, vp]),
+        "ltxb_stage_abort": (None, [vp]),
+        "ltxb_stage_free": (None, [vp]),
         "ltxb_weights_upload": (i32, [i32, vp, u64, vp, i32, i32, i32, i32, i32, i32, ctypes.POINTER(vp)]),
         "ltxb_weights_bytes": (u64, [vp]),
         "ltxb_weights_free": (None, [vp]),
@@ -296,6 +303,69 @@ class Blob:
             if normalize_name(e["name"]) == want:
                 return e
         raise LtxbError(EMISSING, f"blob {self.manifest.get('block')}: no entry named {want}")
+
+
+class _StageStats(ctypes.Structure):
+    _fields_ = [("reader_parks", ctypes.c_uint64), ("consumer_parks", ctypes.c_uint64),
+                ("copy_ns", ctypes.c_uint64), ("verify_ns", ctypes.c_uint64), ("staged_bytes", ctypes.c_uint64)]
+
+
+class Stage:
+    """ltxb_stage: a schedule of opened blobs streamed through two host slots
+    by a reader thread (ltx/loader.zig:176-321's Ring). Take positions in
+    order with `acquire` / `release`, or `upload` a block's weights."""
+
+    def __init__(self, blobs: list, schedule: list, slot_bytes: int | None = None, pinned: bool = True,
+                 verify: bool = True):
+        if any(b._map is None for b in blobs):
+            raise LtxbError(EINVAL, "Stage needs blobs from Blob.open")
+        self._blobs = list(blobs)  # keeps the mappings alive
+        handles = (ctypes.c_void_p * len(blobs))(*[b._map.handle.value for b in blobs])
+        sched = (ctypes.c_int * len(schedule))(*schedule)
+        if slot_bytes is None:
+            slot_bytes = max([len(b.data) for b in blobs] + [1])
+        h = ctypes.c_void_p()
+        _check(lib.ltxb_stage_create(handles, len(blobs), sched, len(schedule), int(slot_bytes), int(pinned),
+                                     int(verify), ctypes.byref(h)))
+        self.handle = h
+        self.schedule = list(schedule)
+
+    def acquire(self, pos: int, timeout_ms: int = 60000) -> memoryview:
+        """The staged bytes of schedule position `pos` (valid until release)."""
+        p, n = ctypes.c_void_p(), ctypes.c_uint64()
+        _check(lib.ltxb_stage_acquire(self.handle, pos, ctypes.byref(p), ctypes.byref(n), int(timeout_ms)))
+        return memoryview((ctypes.c_uint8 * n.value).from_address(p.value)) if n.value else memoryview(b"")
+
+    def release(self, pos: int) -> None:
+        _check(lib.ltxb_stage_release(self.handle, pos))
+
+    def upload(self, pos: int, mode: int = MODE_INT8, qset: int = QSET_REF, hidden: int = 4096, ff: int = 16384,
+               device: int = 0, timeout_ms: int = 60000) -> "Weights":
+        """buildQuantBufs / buildBlockBufs from the slot of position `pos`."""
+        blk = self._blobs[self.schedule[pos]].manifest.get("block", 0)
+        h = ctypes.c_void_p()
+        _check(lib.ltxb_stage_upload(self.handle, pos, device, int(blk), mode, qset, hidden, ff, int(timeout_ms),
+                                     ctypes.byref(h)))
+        return Weights(h, mode, hidden, ff, device, qset)
+
+    def stats(self) -> dict:
+        s = _StageStats()
+        _check(lib.ltxb_stage_get_stats(self.handle, ctypes.byref(s)))
+        return {k: int(getattr(s, k)) for k, _ in _StageStats._fields_}
+
+    def abort(self) -> None:
+        lib.ltxb_stage_abort(self.handle)
+
+    def free(self) -> None:
+        if self.handle:
+            lib.ltxb_stage_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 class Weights:

@@ -16,6 +16,8 @@ two f32 modulation tables.
 from __future__ import annotations
 
 import hashlib
+import json
+import pathlib
 
 ALIGN = 64
 
@@ -86,3 +88,20 @@ def pack(tensors) -> tuple[bytes, list[dict]]:
         entries.append(dict(name=name, dtype=dt, shape=list(shape), offset=off, nbytes=len(data),
                             sha256=hashlib.sha256(data).hexdigest()))
     return bytes(blob), entries
+
+
+def write_dir(directory, tensors, block: int = 0, provenance: dict | None = None) -> dict:
+    """Writes the on-disk unit of tools/pack_block.py:41-99 into `directory`:
+    blob.bin and blob_manifest.json (align, block, total_bytes, blob_sha256,
+    entries with their own sha256, plus `provenance` fields such as repo and
+    revision). Returns the manifest."""
+    d = pathlib.Path(directory)
+    d.mkdir(parents=True, exist_ok=True)
+    blob, entries = pack(tensors)
+    man = dict(packer_version=1, packer_commit="ltxb", align=ALIGN, block=block, repo="", revision="",
+               source_file="", model_version="")
+    man.update(provenance or {})
+    man.update(total_bytes=len(blob), blob_sha256=hashlib.sha256(blob).hexdigest(), entries=entries)
+    (d / "blob.bin").write_bytes(blob)
+    (d / "blob_manifest.json").write_text(json.dumps(man, indent=1))
+    return man
