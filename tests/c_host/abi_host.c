@@ -44,6 +44,27 @@ static void blob_checks(const char* dir) {
   char hex[65];
   ltxb_sha256_hex("abc", 3, hex);
   check(strlen(hex) == 64, "sha256 hex digest");
+
+  /* the staging ring over the same blob, three times, host-memory slots */
+  const ltxb_blob* list[1] = {b};
+  const int schedule[3] = {0, 0, 0};
+  ltxb_stage* st = NULL;
+  check(ltxb_stage_create(list, 1, schedule, 3, bytes, 0, 1, &st) == LTXB_OK && st != NULL, "stage: create");
+  int same = st != NULL;
+  for (int pos = 0; st && pos < 3; ++pos) {
+    const void* slot = NULL;
+    uint64_t got = 0;
+    if (ltxb_stage_acquire(st, pos, &slot, &got, 10000) != LTXB_OK || got != bytes || memcmp(slot, data, bytes))
+      same = 0;
+    if (ltxb_stage_release(st, pos) != LTXB_OK) same = 0;
+  }
+  check(same, "stage: every position holds the blob's bytes");
+  ltxb_stage_stats ss;
+  check(st && ltxb_stage_get_stats(st, &ss) == LTXB_OK && ss.staged_bytes == 3 * bytes, "stage: stats");
+  ltxb_stage_free(st);
+  check(ltxb_stage_create(list, 1, schedule, 3, bytes - 1, 0, 0, &st) == LTXB_EINVAL &&
+            strstr(ltxb_last_error(), "SlotTooSmall") != NULL,
+        "stage: SlotTooSmall");
   ltxb_blob_close(b);
   check(ltxb_blob_open("/nonexistent-blob-dir", 0, &b) == LTXB_EMISSING && b == NULL, "blob: missing directory");
 }
