@@ -637,6 +637,30 @@ std::string normalize(const char* name) {
 
 extern "C" {
 
+// checkLayout (ltx/loader.zig:73-82): aligned offsets, increasing, gaps only
+// alignment fill, the last entry ending at the blob's end. Every entry is
+// also checked to lie inside the blob, so no sum below wraps around.
+int ltxb_blob_check_layout(const ltxb_entry* entries, int n_entries, uint64_t blob_bytes, uint32_t align) {
+  if (n_entries < 0 || (n_entries > 0 && !entries) || align == 0) return set_error(LTXB_EINVAL, "bad arguments");
+  uint64_t end = 0;
+  for (int i = 0; i < n_entries; ++i) {
+    const ltxb_entry& e = entries[i];
+    const char* name = e.name ? e.name : "(unnamed)";
+    if (e.offset % align) return set_error(LTXB_ELAYOUT, "Misaligned: %s at %llu", name, (unsigned long long)e.offset);
+    if (e.offset < end || e.offset - end >= align)
+      return set_error(LTXB_ELAYOUT, "LayoutGap: %s at %llu after %llu", name, (unsigned long long)e.offset,
+                       (unsigned long long)end);
+    if (e.nbytes > blob_bytes || e.offset > blob_bytes - e.nbytes)
+      return set_error(LTXB_ELAYOUT, "TrailingBytes: %s (%llu bytes at %llu) ends past the blob's %llu bytes", name,
+                       (unsigned long long)e.nbytes, (unsigned long long)e.offset, (unsigned long long)blob_bytes);
+    end = e.offset + e.nbytes;
+  }
+  if (end != blob_bytes)
+    return set_error(LTXB_ELAYOUT, "TrailingBytes: entries end at %llu, blob is %llu", (unsigned long long)end,
+                     (unsigned long long)blob_bytes);
+  return LTXB_OK;
+}
+
 int ltxb_blob_open(const char* dir, int verify, ltxb_blob** out) {
   if (!out) return set_error(LTXB_EINVAL, "blob open: out is null");
   *out = nullptr;

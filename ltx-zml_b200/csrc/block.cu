@@ -555,23 +555,6 @@ int ltxb_ring_step(int rank, int nranks, int step, int* compute_shard, int* recv
   return LTXB_OK;
 }
 
-int ltxb_blob_check_layout(const ltxb_entry* entries, int n_entries, uint64_t blob_bytes, uint32_t align) {
-  if (n_entries < 0 || (n_entries > 0 && !entries) || align == 0) return set_error(LTXB_EINVAL, "bad arguments");
-  uint64_t end = 0;
-  for (int i = 0; i < n_entries; ++i) {
-    const ltxb_entry& e = entries[i];
-    if (e.offset % align) return set_error(LTXB_ELAYOUT, "Misaligned: %s at %llu", e.name, (unsigned long long)e.offset);
-    if (e.offset < end || e.offset - end >= align)
-      return set_error(LTXB_ELAYOUT, "LayoutGap: %s at %llu after %llu", e.name, (unsigned long long)e.offset,
-                       (unsigned long long)end);
-    end = e.offset + e.nbytes;
-  }
-  if (end != blob_bytes)
-    return set_error(LTXB_ELAYOUT, "TrailingBytes: entries end at %llu, blob is %llu", (unsigned long long)end,
-                     (unsigned long long)blob_bytes);
-  return LTXB_OK;
-}
-
 void ltxb_weights_free(ltxb_weights* w) {
   if (!w) return;
   int prev = 0;

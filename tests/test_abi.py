@@ -329,3 +329,21 @@ def test_blob_view_outlives_the_blob_object():
     data = ltxb.Blob.open(GOLD, verify_digest=True, verify_entries=True).data
     gc.collect()
     assert bytes(data[:4096]) == (GOLD / "blob.bin").read_bytes()[:4096]
+
+
+def test_layout_check_rejects_entries_past_the_end():
+    """An entry whose offset + nbytes runs past the blob (or wraps a 64-bit
+    sum back into range) is a layout error, never a later out-of-bounds
+    read."""
+    import ltxb
+    names = [ctypes.c_char_p(n) for n in (b"a", b"b", b"c")]
+    arr = (ltxb._Entry * 3)()
+    for e, nm in zip(arr, names):
+        e.name, e.dtype, e.ndim = nm, 1, 1
+    arr[0].offset, arr[0].nbytes = 0, 64
+    arr[1].offset, arr[1].nbytes = 64, (1 << 64) - 64   # 64 + nbytes wraps to 0
+    arr[2].offset, arr[2].nbytes = 0, 128
+    assert ltxb.lib.ltxb_blob_check_layout(ctypes.addressof(arr), 3, 128, 64) == ltxb.ELAYOUT
+    assert "ends past the blob" in ltxb.last_error()
+    arr[1].nbytes = 128                                   # 64 + 128 > 128
+    assert ltxb.lib.ltxb_blob_check_layout(ctypes.addressof(arr), 2, 128, 64) == ltxb.ELAYOUT
