@@ -37,6 +37,8 @@
 // into a running state across the shards of the ring alternative of
 // sequence parallelism; attn_combine_kernel turns the states into the output.
 #define LTXB_LOCAL_STATUS 1  // whole-program device code (no -rdc): own status word
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -579,13 +581,14 @@ __global__ void attn_combine_kernel(const float* __restrict__ o_acc, const float
 
 template <bool MERGE>
 static int launch_attn(const AttnArgs& a, cudaStream_t st) {
-  static bool attr[64] = {};
+  static std::atomic<bool> attr[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
+  if (dev < 0 || dev >= kMaxDevices) return set_error(LTXB_EINVAL, "attention: device %d out of range", dev);
+  if (!attr[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<MERGE>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
     if (e != cudaSuccess) return set_cuda_error(e, "attention: cudaFuncSetAttribute");
-    attr[dev & 63] = true;
+    attr[dev].store(true, std::memory_order_release);
   }
   const int w = a.H * AT_D;
   CUtensorMap tq, tk, tv;

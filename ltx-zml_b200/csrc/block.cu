@@ -197,10 +197,11 @@ static int run_lin(const LinCall& lc, const Lin& L, const void* A, int lda, int 
     } else {
       if ((size_t)L.N * L.K > lc.b->deq_elems)
         return set_error(LTXB_EINVAL, "int8 linear [%d, %d] exceeds the expansion buffer", L.N, L.K);
-      int rc = dequant_weights(L.wq, L.sc, L.sc_bf16, L.N, L.K, lc.b->deq, lc.st);
-      if (rc) return rc;
       g.B = lc.b->deq;
       g.ldb = L.K;
+      if (int rc = gemm_check(g, nullptr)) return rc;
+      int rc = dequant_weights(L.wq, L.sc, L.sc_bf16, L.N, L.K, lc.b->deq, lc.st);
+      if (rc) return rc;
     }
   } else {
     g.B = L.w;
@@ -577,7 +578,9 @@ int ltxb_weights_upload(int device, const void* blob, uint64_t blob_bytes, const
     return set_error(LTXB_EINVAL, "unknown quant set %d", qset);
   if (hidden <= 0 || hidden % 256 || ff <= 0 || ff % 256)
     return set_error(LTXB_EINVAL, "hidden (%d) and ff (%d) must be positive multiples of 256", hidden, ff);
-  int rc = ltxb_init(device);
+  int rc = check_entries(entries, n_entries, blob_bytes);
+  if (rc) return rc;
+  rc = ltxb_init(device);
   if (rc) return rc;
   auto* w = new ltxb_weights();
   w->device = device;
@@ -918,10 +921,15 @@ int ltxb_dq_gemm(const void* A, const void* Wq, const void* scales, int scale_dt
   } else {
     if (!workspace || workspace_bytes < (uint64_t)N * K * 2)
       return set_error(LTXB_EINVAL, "dq_gemm: unfused path needs N*K*2 workspace bytes");
-    int rc = dequant_weights(static_cast<const int8_t*>(Wq), scales, scale_dtype == LTXB_DT_BF16, N, K, workspace, st);
-    if (rc) return rc;
     g.B = workspace;
     g.ldb = K;
+    // all checks before the expansion launch
+    if (int rc = gemm_check(g, nullptr)) return rc;
+    if ((reinterpret_cast<uintptr_t>(Wq) & 15) ||
+        (reinterpret_cast<uintptr_t>(scales) & (scale_dtype == LTXB_DT_BF16 ? 1 : 3)))
+      return set_error(LTXB_EINVAL, "dq_gemm: weights must be 16-byte aligned, scales element-aligned");
+    int rc = dequant_weights(static_cast<const int8_t*>(Wq), scales, scale_dtype == LTXB_DT_BF16, N, K, workspace, st);
+    if (rc) return rc;
   }
   return gemm_tc(g, st);
 }

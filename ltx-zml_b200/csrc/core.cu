@@ -282,6 +282,7 @@ int ltxb_core_upload(int device, const void* blob, uint64_t blob_bytes, const lt
   if (!out || !blob || !entries || n_entries <= 0) return set_error(LTXB_EINVAL, "core upload: null argument");
   if (hidden <= 0 || hidden % 128) return set_error(LTXB_EINVAL, "core upload: hidden must be a multiple of 128");
   *out = nullptr;
+  if (int rc0 = check_entries(entries, n_entries, blob_bytes)) return rc0;
   cudaError_t ce = cudaSetDevice(device);
   if (ce != cudaSuccess) return set_cuda_error(ce, "cudaSetDevice");
   auto* c = new ltxb_core();

@@ -5,6 +5,8 @@
 // epilogues, and a blockwise online-softmax attention (whileSdpa,
 // ltx/block.zig:105-154). They serve the 1k-token conformance config and
 // full-size cross-checks of the tensor-core path; throughput is not their job.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -225,13 +227,14 @@ int attention_f32(const float* q, int ldq, const float* k, int ldk, const float*
   if (Tkv <= 0) return set_error(LTXB_EINVAL, "attention_f32: empty K/V");
   const size_t smem =
       sizeof(float) * (FA_Q * FA_D + FA_K * (FA_D + 1) + FA_K * FA_D + FA_Q * (FA_K + 1) + 2 * FA_Q);
-  static bool attr[64] = {};
+  static std::atomic<bool> attr[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
+  if (dev < 0 || dev >= kMaxDevices) return set_error(LTXB_EINVAL, "attention_f32: device %d out of range", dev);
+  if (!attr[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(attention_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_cuda_error(e, "attention_f32 attr");
-    attr[dev & 63] = true;
+    attr[dev].store(true, std::memory_order_release);
   }
   dim3 grid((Tq + FA_Q - 1) / FA_Q, H);
   attention_f32_kernel<<<grid, 256, smem, st>>>(q, ldq, k, ldk, v, ldv, out, gate, ldg, Tq, Tkv, H, scale);

@@ -16,6 +16,8 @@
 //               bf16 tile in the 128B-swizzled K-major layout the MMA reads
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the main loop of tile i+1.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -323,13 +325,16 @@ template <int BN, bool BQ8, int EPI>
 static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
   using C = GemmCfg<BN, BQ8>;
   auto kern = gemm_tc_kernel<BN, BQ8, EPI>;
-  static bool attr_set[64] = {};
+  // per device and instance: the shared-memory opt-in, set once (host threads
+  // may race to set it; the call is idempotent and the flag is atomic)
+  static std::atomic<bool> attr_set[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
+  if (dev < 0 || dev >= kMaxDevices) return set_error(LTXB_EINVAL, "gemm: device %d out of range", dev);
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return set_cuda_error(e, "gemm: cudaFuncSetAttribute");
-    attr_set[dev & 63] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const int num_tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * (a.N / BN);
   const int grid = num_tiles < sm_count() ? num_tiles : sm_count();
@@ -353,7 +358,7 @@ static int dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   return set_error(LTXB_EINVAL, "gemm: unknown epilogue");
 }
 
-int gemm_tc(const GemmArgs& a, cudaStream_t st) {
+int gemm_check(const GemmArgs& a, int* bn_out) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return set_error(LTXB_EINVAL, "gemm: empty shape");
   if (a.K % GEMM_BK) return set_error(LTXB_EINVAL, "gemm: K must be a multiple of 64");
   if (a.b_int8 && (a.K % 128)) return set_error(LTXB_EINVAL, "gemm: int8 weights need K % 128 == 0");
@@ -368,6 +373,13 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st) {
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!a16(a.out) || !a16(a.bias) || !a16(a.xres) || (a.xres && a.ldx % 4))
     return set_error(LTXB_EINVAL, "gemm: out, bias and residual must be 16-byte aligned");
+  if (bn_out) *bn_out = bn;
+  return LTXB_OK;
+}
+
+int gemm_tc(const GemmArgs& a, cudaStream_t st) {
+  int bn = 0;
+  if (int rc = gemm_check(a, &bn)) return rc;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda, GEMM_BK, GEMM_BM,
                         CU_TENSOR_MAP_SWIZZLE_128B);

@@ -16,6 +16,8 @@ int set_cuda_error(cudaError_t e, const char* what);
 // LTXB_EINVAL unless `device` (where a handle's buffers live) is the current device
 int check_device(int device, const char* what);
 int sm_count();
+// per-device caches are indexed by device ordinal below this bound
+constexpr int kMaxDevices = 64;
 
 // ---- launch accounting and per-phase profiling ----
 // Every kernel launcher calls launched() after a successful launch, so
@@ -75,6 +77,9 @@ struct GemmArgs {
   int ada_row;
   int ada_d;
 };
+// Shape, alignment and tile checks of gemm_tc, on the host, launching
+// nothing; *bn_out receives the N tile gemm_tc will use.
+int gemm_check(const GemmArgs& a, int* bn_out);
 int gemm_tc(const GemmArgs& a, cudaStream_t st);
 
 // ---- flash attention (tcgen05) ----

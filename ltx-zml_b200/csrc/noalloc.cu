@@ -55,8 +55,6 @@ extern "C" int ltxb_dq_gemm_noalloc(const void* A, const void* Wq, const void* s
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = dequant_weights(static_cast<const int8_t*>(Wq), scales, scale_dtype == LTXB_DT_BF16, N, K, scratch, st);
-  if (rc) return rc;
   GemmArgs g{};
   g.A = A;
   g.lda = K;
@@ -69,5 +67,12 @@ extern "C" int ltxb_dq_gemm_noalloc(const void* A, const void* Wq, const void* s
   g.bias = bias;
   g.out = out;
   g.ldo = N;
+  // every argument check runs before the first launch: a rejected call
+  // leaves the shared scratch untouched
+  if ((rc = gemm_check(g, nullptr))) return rc;
+  if ((reinterpret_cast<uintptr_t>(Wq) & 15) || (reinterpret_cast<uintptr_t>(scales) & (scale_dtype == LTXB_DT_BF16 ? 1 : 3)))
+    return set_error(LTXB_EINVAL, "dq_gemm_noalloc: weights must be 16-byte aligned, scales element-aligned");
+  rc = dequant_weights(static_cast<const int8_t*>(Wq), scales, scale_dtype == LTXB_DT_BF16, N, K, scratch, st);
+  if (rc) return rc;
   return gemm_tc(g, st);
 }

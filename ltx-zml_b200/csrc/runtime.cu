@@ -32,18 +32,18 @@ int set_cuda_error(cudaError_t e, const char* what) {
   return set_error(LTXB_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }
 
-static int g_sms[64];
+static std::atomic<int> g_sms[kMaxDevices];
 
 int sm_count() {
   int dev = 0;
   cudaGetDevice(&dev);
-  dev &= 63;
-  if (g_sms[dev] == 0) {
-    int n = 0;
+  const bool cached = dev >= 0 && dev < kMaxDevices;
+  int n = cached ? g_sms[dev].load(std::memory_order_relaxed) : 0;
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_sms[dev] = n;
+    if (cached) g_sms[dev].store(n, std::memory_order_relaxed);
   }
-  return g_sms[dev];
+  return n;
 }
 
 // ---- launch accounting / profiling ----

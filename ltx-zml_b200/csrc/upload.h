@@ -40,6 +40,18 @@ inline std::string norm_name(const char* n) {
   return s;
 }
 
+// Every caller-supplied entry must lie inside the blob: offset + nbytes <=
+// blob_bytes, checked in a form no 64-bit sum can wrap. Runs on the host
+// before any device call, so a bad table is rejected without touching a GPU.
+inline int check_entries(const ltxb_entry* e, int n, uint64_t blob_bytes) {
+  for (int i = 0; i < n; ++i)
+    if (e[i].nbytes > blob_bytes || e[i].offset > blob_bytes - e[i].nbytes)
+      return set_error(LTXB_ELAYOUT, "entry %d (%s): %llu bytes at %llu run past the %llu-byte blob", i,
+                       e[i].name ? e[i].name : "?", (unsigned long long)e[i].nbytes,
+                       (unsigned long long)e[i].offset, (unsigned long long)blob_bytes);
+  return LTXB_OK;
+}
+
 // Finds, checks and uploads the tensors of one weight set from a host blob:
 // entries are named `<prefix><stem>` (prefix "transformer_blocks_<i>_" for a
 // block, empty for the core parts); every allocation is recorded in `allocs`
@@ -81,7 +93,8 @@ struct Uploader {
                        x->dtype, (long long)rows, (long long)cols, dtype, (long long)r, (long long)c);
     const int esz = dtype == LTXB_DT_F32 ? 4 : dtype == LTXB_DT_BF16 ? 2 : 1;
     const uint64_t need = (uint64_t)r * (c ? c : 1) * esz;
-    if (x->nbytes != need || x->offset + x->nbytes > blob_bytes)
+    // written so that no sum can wrap: offset + nbytes <= blob_bytes
+    if (x->nbytes != need || x->nbytes > blob_bytes || x->offset > blob_bytes - x->nbytes)
       return set_error(LTXB_ELAYOUT, "entry %s: %llu bytes at %llu does not fit (need %llu, blob %llu)", x->name,
                        (unsigned long long)x->nbytes, (unsigned long long)x->offset, (unsigned long long)need,
                        (unsigned long long)blob_bytes);

@@ -347,3 +347,25 @@ def test_layout_check_rejects_entries_past_the_end():
     assert "ends past the blob" in ltxb.last_error()
     arr[1].nbytes = 128                                   # 64 + 128 > 128
     assert ltxb.lib.ltxb_blob_check_layout(ctypes.addressof(arr), 2, 128, 64) == ltxb.ELAYOUT
+
+
+@pytest.mark.parametrize("offset,nbytes", [((1 << 64) - 8, 64), (0, (1 << 64) - 1), (64, 128)])
+def test_upload_rejects_entries_past_the_blob_before_any_device_call(offset, nbytes):
+    """ltxb_weights_upload and ltxb_core_upload take caller-built entry tables.
+    An entry whose offset + nbytes leaves the blob, including one whose 64-bit
+    sum wraps back into range (offset = 2^64 - 8), is ELAYOUT, decided on the
+    host before any device call, so no copy ever reads outside the blob."""
+    import ltxb
+    blob = (ctypes.c_uint8 * 128)()
+    arr = (ltxb._Entry * 1)()
+    arr[0].name, arr[0].dtype, arr[0].ndim = b"transformer_blocks_0_attn1_to_q_weight", 1, 2
+    arr[0].shape[0], arr[0].shape[1] = 4, 8
+    arr[0].offset, arr[0].nbytes = offset, nbytes
+    h = ctypes.c_void_p()
+    rc = ltxb.lib.ltxb_weights_upload(0, ctypes.addressof(blob), 128, ctypes.addressof(arr), 1, 0, ltxb.MODE_BF16,
+                                      0, 256, 256, ctypes.byref(h))
+    assert rc == ltxb.ELAYOUT, ltxb.last_error()
+    assert "past the 128-byte blob" in ltxb.last_error()
+    assert not h.value
+    rc = ltxb.lib.ltxb_core_upload(0, ctypes.addressof(blob), 128, ctypes.addressof(arr), 1, 256, ctypes.byref(h))
+    assert rc == ltxb.ELAYOUT, ltxb.last_error()

@@ -78,3 +78,46 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(cuda):
             torch.cuda.current_stream().cuda_stream)
     assert rc == ltxb.EINVAL
     assert "scratch" in ltxb.last_error()
+
+
+def test_noalloc_calls_allocate_no_device_memory(cuda):
+    """The property the entry point exists for: once its first call on the
+    device has looked up the scratch address (and the driver has loaded the
+    kernels), further calls leave the device's free memory unchanged."""
+    fn = _noalloc_fn()
+    a, wq, s, b = _case(256, 2048, 4096, 13, "bf16", cuda)
+    out = torch.empty(256, 2048, dtype=torch.bfloat16, device=cuda)
+    st = torch.cuda.current_stream().cuda_stream
+    import ltxb
+
+    def call():
+        rc = fn(a.data_ptr(), wq.data_ptr(), s.data_ptr(), ltxb.DT_BF16, b.data_ptr(), out.data_ptr(), 256, 2048,
+                4096, st)
+        assert rc == ltxb.OK, ltxb.last_error()
+
+    call()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(cuda)
+    reserved0 = torch.cuda.memory_reserved(cuda)
+    for _ in range(5):
+        call()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(cuda)
+    assert free1 == free0
+    assert torch.cuda.memory_reserved(cuda) == reserved0
+    assert ltxb.device_status() == ltxb.OK
+
+
+def test_noalloc_rejects_bad_arguments_before_launching(cuda):
+    """A call that ends in EINVAL (here a misaligned output) launches nothing,
+    so it cannot overwrite the shared scratch under another caller's call."""
+    import ltxb
+    fn = _noalloc_fn()
+    a, wq, s, b = _case(128, 1024, 2048, 14, "f32", cuda)
+    out = torch.empty(128 * 1024 + 8, dtype=torch.bfloat16, device=cuda)
+    n0 = ltxb.launch_count()
+    rc = fn(a.data_ptr(), wq.data_ptr(), s.data_ptr(), ltxb.DT_F32, b.data_ptr(), out.data_ptr() + 2, 128, 1024, 2048,
+            torch.cuda.current_stream().cuda_stream)
+    assert rc == ltxb.EINVAL
+    assert "aligned" in ltxb.last_error()
+    assert ltxb.launch_count() == n0
