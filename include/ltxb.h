@@ -461,6 +461,16 @@ uint64_t ltxb_denoise_workspace_bytes(const ltxb_core* core, const ltxb_weights*
 int ltxb_denoise_run(const ltxb_core* core, const ltxb_weights* const* blocks, int n_blocks, const float* sigmas,
                      int n_steps, const ltxb_denoise_io* io, const ltxb_config* cfg, void* stream);
 
+/* ---- structural statistics (statsOf, ltx/core_parts.zig:183-193) ----
+ * out (3 device floats) = [NaN count (v != v), sum of v^2, max |v| over the
+ * non-NaN values] of the n f32 values at v, so a host checks a full-length
+ * output (the production pass's velocity, ltx/e2e_prod.zig:444-468) with a
+ * 12-byte readback. Sum of squares in f64, rounded once; a fixed grid and
+ * reduction order make the result identical run to run. workspace: at least
+ * ltxb_stats_workspace_bytes() bytes of device memory, 16-byte aligned. */
+uint64_t ltxb_stats_workspace_bytes(void);
+int ltxb_stats(const float* v, uint64_t n, float* out, void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* Size of the scratch ltxb_dq_gemm_noalloc keeps in the library image. */
 #define LTXB_NOALLOC_SCRATCH_BYTES (32u << 20)
 

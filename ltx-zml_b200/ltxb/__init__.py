@@ -118,6 +118,8 @@ def _load() -> ctypes.CDLL:
         "ltxb_attention_split": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, vp, u64, vp]),
         "ltxb_dq_gemm": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, vp, u64, vp]),
         "ltxb_gemm_bf16": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
+        "ltxb_stats_workspace_bytes": (u64, []),
+        "ltxb_stats": (i32, [vp, u64, vp, vp, u64, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -849,6 +851,17 @@ def dq_gemm(a, wq, scales, bias=None, fused: bool = True, out=None, workspace=No
     _check(lib.ltxb_dq_gemm(_ptr(a), _ptr(wq), _ptr(scales), sdt, _ptr(bias), _ptr(out), M, N, K, int(fused),
                             _ptr(workspace), 0 if workspace is None else workspace.numel(), _stream(stream)))
     return out
+
+
+def stats_of(v, stream=None) -> tuple[float, float, float]:
+    """statsOf (ltx/core_parts.zig:183-193) on the device: (NaN count, sum of
+    squares, max |v|) of an f32 tensor, read back as three floats."""
+    v = v.contiguous()
+    out = torch.empty(3, dtype=torch.float32, device=v.device)
+    ws = torch.empty(int(lib.ltxb_stats_workspace_bytes()), dtype=torch.uint8, device=v.device)
+    _check(lib.ltxb_stats(_ptr(v), v.numel(), _ptr(out), _ptr(ws), ws.numel(), _stream(stream)))
+    n, ss, ma = out.cpu().tolist()
+    return n, ss, ma
 
 
 def gemm_bf16(a, w, bias=None, out=None, stream=None) -> torch.Tensor:

@@ -102,3 +102,41 @@ def check_layout(entries: list[Entry], total: int, align: int = ALIGN) -> None:
         end = e.offset + e.nbytes
     if end != total:
         raise ValueError("TrailingBytes")
+
+
+def block_weights_from_blob(data: bytes, entries, geom: ref.Geometry, block_idx: int = 0) -> ref.BlockWeights:
+    """The inverse of block_tensors: one block's tensors read back from a
+    packed blob (entries as dicts or Entry objects, names as the reference's
+    loader finds them, ltx/loader.zig:102-129). A quantised field may be
+    stored without its bf16 original (`name::q8` + `name::q8scale` only);
+    its float tensor is then the exact f64 dequantisation."""
+    import torch
+    by_name = {}
+    for e in entries:
+        g = (lambda k: e[k]) if isinstance(e, dict) else (lambda k: getattr(e, k))
+        by_name[normalize_name(g("name"))] = (g("dtype"), list(g("shape")), g("offset"), g("nbytes"))
+
+    def read(key):
+        dt, shape, off, nb = by_name[key]
+        raw = np.frombuffer(data, dtype=np.uint8, count=nb, offset=off)
+        npdt = {"BF16": np.uint16, "F32": np.float32, "I8": np.int8}[dt]
+        return raw.view(npdt).reshape(shape).copy(), dt
+
+    bw = ref.BlockWeights(geom=geom)
+    for field_, dotted in DOTTED.items():
+        key = normalize_name(f"transformer_blocks.{block_idx}.{dotted}")
+        if key + "_q8" in by_name:
+            q, _ = read(key + "_q8")
+            sc, _ = read(key + "_q8scale")
+            bw.raw[field_ + "::q8"] = q
+            bw.raw[field_ + "::q8scale"] = sc
+        if key in by_name:
+            a, dt = read(key)
+            bw.raw[field_] = a
+            f = a if dt == "F32" else ref.bf16_to_f32(a)
+            bw.t[field_] = torch.from_numpy(f.astype(np.float64))
+        elif field_ + "::q8" in bw.raw:
+            bw.t[field_] = torch.from_numpy(ref.dequant(bw.raw[field_ + "::q8"], bw.raw[field_ + "::q8scale"]))
+        else:
+            raise KeyError(f"blob has no entry {key}")
+    return bw

@@ -20,7 +20,9 @@ traced block, `ltx/block.zig`, op for op:
   Block.attention  ltx/block.zig:212-244  qk-norm over full D, RoPE, SDPA,
                                           2*sigmoid per-head gate, out-proj
   Block stages     ltx/block.zig:248-353  s1 ... s7, block_out, w_block_out,
-                                          w_attn1, f_logits
+                                          w_attn1, f_logits; staged_rows (the
+                                          stages on sampled query rows of a
+                                          full-length input)
   dq / lin_q       ltx/block.zig:462-477  int8 grouped-128 dequant linear
   QBlock           ltx/block.zig:481-611  the block on dequantised weights of a
                                           field set: q_block_out_all (q/k/v x2 +
@@ -164,7 +166,7 @@ def while_sdpa_c(chunk: int, q3: torch.Tensor, k3: torch.Tensor, v3: torch.Tenso
         cmax = s.amax(dim=-1)
         m_new = torch.maximum(m, cmax)
         corr = torch.exp(m - m_new)
-        p = torch.exp(s - m_new[..., None])
+        p = s.sub_(m_new[..., None]).exp_()   # exp(s - m_new), in the score buffer
         l = l * corr + p.sum(dim=-1)
         acc = acc * corr[..., None] + torch.einsum("hqk,khd->hqd", p, vc)
         m = m_new
@@ -432,6 +434,53 @@ class Block:
         ff = self.ffn(ff_in)
         out["s7_ff_out"] = ff
         out["block_out"] = x_ca + ff * ada_val(self.w["sst"], tstab, tidx, 5)
+        return out
+
+
+    def staged_rows(self, x, tstab, tidx, ctx, pts2, cos, sin, rows, head_group: int = 8):
+        """`staged` for the query rows `rows` only (a full-length run checked
+        on sampled rows). Every stage of ltx/block.zig:248-353 is per token
+        except self-attention, whose keys and values come from all T tokens:
+        K = rope(rmsW(lin(n, k1)), cos, sin) and V = lin(n, v1) are computed
+        over every row (ltx/block.zig:212-231), the queries only for `rows`
+        with those rows' cos/sin. Dense softmax over all T keys, `head_group`
+        heads at a time to bound the score buffer. Returns
+        {stage: [len(rows), D]}."""
+        w = self.w
+        rows = torch.as_tensor(np.asarray(rows), dtype=torch.long)
+        n_all = self.s1_norm_msa(x, tstab, tidx)
+        k_all = rope(rms_w(lin(n_all, w["k1_w"], w["k1_b"]), w["kn1"]), cos, sin)
+        v_all = lin(n_all, w["v1_w"], w["v1_b"])
+        n = n_all[rows]
+        del n_all
+        xr, tr = x[rows], tidx[rows]
+        out = {"s1_norm_msa": n}
+        qn = rms_w(lin(n, w["q1_w"], w["q1_b"]), w["qn1"])
+        out["s1b_qnorm"] = qn
+        q = rope(qn, cos[rows], sin[rows])
+        r, t = q.shape[0], k_all.shape[0]
+        q3 = q.reshape(r, self.h, HD)
+        k3 = k_all.reshape(t, self.h, HD)
+        v3 = v_all.reshape(t, self.h, HD)
+        att = torch.cat([sdpa_dense(q3[:, h0:h0 + head_group], k3[:, h0:h0 + head_group],
+                                    v3[:, h0:h0 + head_group]) for h0 in range(0, self.h, head_group)], dim=1)
+        del k_all, v_all, k3, v3
+        out["s2_attn1_nogate"] = lin(att.reshape(r, self.h * HD), w["o1_w"], w["o1_b"])
+        gate = torch.sigmoid(lin(n, w["g1_w"], w["g1_b"])) * 2.0           # ltx/block.zig:236-240
+        a1 = lin((att * gate[:, :, None]).reshape(r, self.h * HD), w["o1_w"], w["o1_b"])
+        out["s3_attn1"] = a1
+        x_sa = xr + a1 * ada_val(w["sst"], tstab, tr, 2)
+        out["s4_after_sa"] = x_sa
+        xn = rms_no_w(x_sa)
+        out["s4_normed"] = xn
+        ca = self.ca_out(xn, tstab, tr, ctx, pts2)
+        out["s5_ca_out"] = ca
+        x_ca = x_sa + ca
+        ff_in = modulate(rms_no_w(x_ca), ada_val(w["sst"], tstab, tr, 4), ada_val(w["sst"], tstab, tr, 3))
+        out["s6_ff_in"] = ff_in
+        ff = self.ffn(ff_in)
+        out["s7_ff_out"] = ff
+        out["block_out"] = x_ca + ff * ada_val(w["sst"], tstab, tr, 5)
         return out
 
 

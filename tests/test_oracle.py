@@ -242,3 +242,37 @@ def test_logits_and_blockwise_attn1():
     want = ref.lin(core, blk.w["o1_w"], blk.w["o1_b"])
     assert ref.rel_rms(want, blk.s2_attn1_nogate(x, tstab, tidx, cos, sin)) < 1e-12
     assert ref.rel_rms(blk.w_attn1(x, tstab, tidx, cos, sin), blk.s3_attn1(x, tstab, tidx, cos, sin)) < 1e-12
+
+
+def test_staged_rows_equals_staged_on_those_rows():
+    """The sampled-rows restatement used at full length equals the one-pass
+    staged block on the same rows (K/V over all tokens, queries on the
+    sample), in f64, on int8 EXT weights with bf16 scales."""
+    geom = ref.Geometry(d=256, ff=512)
+    bw = oin.make_weights(geom, 3, quant="int8", scale_dtype="bf16", qset=ref.Q8_FIELDS_EXT)
+    inp = oin.make_inputs(geom, grid=(2, 4, 16), s=16, seed=3, adaln="random", k_rows=3)
+    blk = ref.QBlock(bw, qset=ref.Q8_FIELDS_EXT)
+    args = inp.torch()
+    full = blk.staged(*args)
+    rows = np.array([0, 5, 63, 64, 100, 127])
+    part = blk.staged_rows(*args, rows=rows, head_group=1)
+    for s in ref.STAGES:
+        assert ref.rel_rms(part[s].numpy(), full[s][rows].numpy()) < 1e-12, s
+
+
+def test_block_weights_read_back_from_a_blob():
+    """oracle.blob.block_weights_from_blob inverts block_tensors + pack: the
+    stored bytes come back exactly, and a quantised field stored without its
+    bf16 original is its exact dequantisation."""
+    from oracle import blob as oblob
+    geom = ref.Geometry(d=256, ff=512)
+    bw = oin.make_weights(geom, 4, quant="int8", scale_dtype="bf16", qset=ref.Q8_FIELDS_EXT)
+    data, ent = oblob.pack(oblob.block_tensors(bw, 0))
+    back = oblob.block_weights_from_blob(data, ent, geom)
+    for k, v in bw.raw.items():
+        assert np.array_equal(back.raw[k], v), k
+    drop = {oblob.normalize_name("transformer_blocks.0." + oblob.DOTTED["o1_w"])}
+    data2, ent2 = oblob.pack([t for t in oblob.block_tensors(bw, 0) if oblob.normalize_name(t[0]) not in drop])
+    back2 = oblob.block_weights_from_blob(data2, ent2, geom)
+    want = ref.dequant(bw.raw["o1_w::q8"], bw.raw["o1_w::q8scale"])
+    assert np.array_equal(back2.t["o1_w"].numpy(), want)
