@@ -3,8 +3,9 @@
 (22x32x40 latent grid, D 4096, 32x128 heads, FFN 16384,
 128 text tokens, int8 grouped-128 weights with bf16 scales for the q/k/v,
 output and FFN projections), on 1..N B200s of one node with the tokens
-sharded across ranks (sequence-parallel self-attention: a head-group
-pipelined K/V all-gather over NVLink, NCCL).
+sharded across ranks (sequence-parallel self-attention: a head-parallel
+all-to-all of q/k/v over NVLink with NCCL, each rank attending its H/N heads
+over all tokens).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -148,39 +149,13 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 def make_blob(device, seed: int = 0, block: int = 0):
-    """Config-3 weights: N(0, 0.02) (norm weights 1 + N(0, 0.02), tables f32),
-    int8 g128 for the extended set (q/k/v/o of both attentions and the FFN)
-    after scaling 0.5% of input channels x20,
-    symmetric absmax/127 scales rounded to bf16; packed in the reference blob
-    format (name-sorted, 64-byte aligned) by the library's writer."""
+    """Config-3 weights (ltxb.blobfmt.synthetic_block): N(0, 0.02) (norm
+    weights 1 + N(0, 0.02), tables f32), int8 g128 for the extended set
+    (q/k/v/o of both attentions and the FFN) after scaling 0.5% of input
+    channels x20, symmetric absmax/127 scales rounded to bf16; packed in the
+    reference blob format (name-sorted, 64-byte aligned)."""
     from ltxb import blobfmt
-    g = torch.Generator(device=device)
-    tensors = []
-    for i, (suffix, spec, dt) in enumerate(blobfmt.BLOCK_TENSORS):
-        shape = blobfmt.shape_of(spec, D, FF)
-        g.manual_seed(seed * 1000 + i)
-        w = torch.randn(*shape, generator=g, device=device) * 0.02
-        name = f"transformer_blocks.{block}.{suffix}"
-        if dt == "F32":
-            tensors.append((name, "F32", shape, w.cpu().numpy().tobytes()))
-            continue
-        if "norm" in suffix:
-            w = w + 1.0
-        if suffix in blobfmt.Q8_EXT:
-            k = shape[1]
-            cols = torch.randperm(k, generator=g, device=device)[: max(1, round(0.005 * k))]
-            w[:, cols] *= 20.0
-            wg = w.view(shape[0], k // 128, 128)
-            amax = wg.abs().amax(-1, keepdim=True)
-            sc = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax)).to(torch.bfloat16)
-            q = torch.clamp(torch.round(wg / sc.float()), -128, 127).to(torch.int8).view(shape)
-            tensors.append((name + "::q8", "I8", shape, q.cpu().numpy().tobytes()))
-            tensors.append((name + "::q8scale", "BF16", [shape[0], k // 128],
-                            sc.view(torch.int16).view(shape[0], k // 128).cpu().numpy().tobytes()))
-        else:
-            tensors.append((name, "BF16", shape, w.to(torch.bfloat16).view(torch.int16).cpu().numpy().tobytes()))
-    data, entries = blobfmt.pack(tensors)
-    return data, entries
+    return blobfmt.synthetic_block(device, D, FF, seed=seed, block=block)
 
 
 def make_inputs(device, rank: int, world: int, seed: int = 0):
@@ -449,8 +424,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 if top in tj:
                     roofline["traffic"] = tj[top]["bytes_per_launch"]
             roofline["peak_source"] = pk["source"] + " (MEASURED_PEAKS.json; sustained for a kernel inside a long step)"
-        sp_algo = ("send/recv ring" if os.environ.get("LTXB_SP_RING") == "1"
-                   else "head-group pipelined K/V all-gather")
+        env_sp = "ring" if os.environ.get("LTXB_SP_RING") == "1" else os.environ.get("LTXB_SP", "alltoall")
+        sp_algo = {"ring": "send/recv ring of K/V shards", "allgather": "head-group pipelined K/V all-gather"}.get(
+            env_sp, "head-parallel all-to-all: q/k/v to the ranks owning their heads, outputs back")
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",

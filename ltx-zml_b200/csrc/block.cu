@@ -12,9 +12,10 @@
 //   5  o    = softmax(q k^T / sqrt(128)) v * gate            attention (ring for SP)
 //   6  x_sa = x + (o . Wo^T + bo) * ada2                      gemm  (resid epilogue)
 //   7  a    = rms(x_sa) (1 + ada7) + ada6                     norm_modulate
-//   8  enc  = ctx (1 + kv1) + kv0;  [k2;v2] = enc . W^T + b    ctx_modulate + gemm (M = S)
+//   8  enc  = ctx (1 + kv1) + kv0;  [k2;v2] = enc . W^T + b    ctx_modulate, split, gemm (M = S,
+//      k2 = rms_w(k2) -> bf16, v2 -> bf16                       f32-exact), f32 q/k norm, cast
 //   9  q2   = a . Wq2^T + b;  gate2                           gemm x2
-//  10  q2,k2 = rms_w(.)                                       qk_norm_rope (no RoPE)
+//  10  q2   = rms_w(.)                                        qk_norm_rope (no RoPE)
 //  11  o2   = cross attention * gate2                          attention (T_kv = S)
 //  12  x_ca = x_sa + (o2 . Wo2^T + b) * ada8                  gemm
 //  13  f    = rms(x_ca) (1 + ada4) + ada3                      norm_modulate
@@ -81,6 +82,9 @@ struct Bufs {
   void* kv2 = nullptr;    // [S, 2D]
   float* ssq2 = nullptr;  // [S, 32]
   void* k2 = nullptr;     // [S, D]
+  float* enc32 = nullptr; // [S, D]   f32 prompt K/V input (tensor-core modes)
+  void* enc_split = nullptr; // [S, 3D] bf16 parts of enc32 (hi | lo | hi)
+  float* kv2_32 = nullptr;// [S, 2D]  f32 prompt K/V projections (tensor-core modes)
   float* x_ca = nullptr;  // [T, D]
   void* h = nullptr;      // [T, FF]
   void* deq = nullptr;    // bf16: the int8 weights of one linear expanded (unfused int8 path)
@@ -88,26 +92,52 @@ struct Bufs {
   float* o_acc = nullptr; // [T, D]  ring state
   float* m_st = nullptr;  // [H, T]
   float* l_st = nullptr;  // [H, T]
+  // head-parallel exchange (SP_ALLTOALL)
+  void* a2a_send = nullptr;  // [3][N][T][D/N] bf16: q, k, v by head group
+  void* a2a_recv = nullptr;  // [3][N T][D/N]: this rank's heads over all tokens
+  void* a2a_o = nullptr;     // [N T][D/N]: their attention output
+  void* a2a_orecv = nullptr; // [N][T][D/N]: this rank's tokens, every head group
+  float* gate_all = nullptr; // [N T][G]
 };
 
 static bool g_fused_dequant = false;  // int8 GEMMs: dequantise in smem (true) or expand first (false)
 
-// Sequence-parallel self-attention: all-gather of K/V (default) or the ring
-// of send/recv steps (LTXB_SP_RING=1, kept for comparison).
-static bool sp_use_ring() {
-  static const bool ring = [] {
-    const char* e = getenv("LTXB_SP_RING");
-    return e && e[0] == '1';
+// Sequence-parallel self-attention, three exchanges:
+//   SP_ALLTOALL  head-parallel: q/k/v go to the rank that owns their heads
+//                (H/N heads per rank, all tokens), the outputs come back;
+//                the default when the heads divide evenly over the ranks
+//   SP_ALLGATHER every rank gathers all K/V, head group by head group, and
+//                attends its own tokens (LTXB_SP=allgather)
+//   SP_RING      K/V shards passed around a ring (LTXB_SP=ring or
+//                LTXB_SP_RING=1), kept for comparison
+enum SpAlgo { SP_ALLTOALL = 0, SP_ALLGATHER = 1, SP_RING = 2 };
+static int sp_env_algo() {
+  static const int a = [] {
+    const char* r = getenv("LTXB_SP_RING");
+    if (r && r[0] == '1') return (int)SP_RING;
+    const char* e = getenv("LTXB_SP");
+    if (e && !strcmp(e, "ring")) return (int)SP_RING;
+    if (e && !strcmp(e, "allgather")) return (int)SP_ALLGATHER;
+    if (e && !strcmp(e, "alltoall")) return (int)SP_ALLTOALL;
+    return -1;
   }();
-  return ring;
+  return a;
 }
+static SpAlgo sp_algo(const ltxb_weights* w, const ltxb_config* c) {
+  const int n = c->sp_size > 1 ? c->sp_size : 1;
+  const bool a2a_ok = w->H % n == 0;
+  const int e = sp_env_algo();
+  if (e == SP_RING || e == SP_ALLGATHER) return static_cast<SpAlgo>(e);
+  return a2a_ok ? SP_ALLTOALL : SP_ALLGATHER;
+}
+static bool sp_use_ring(const ltxb_weights* w, const ltxb_config* c) { return sp_algo(w, c) == SP_RING; }
 // K/V splits of the gathered attention (1 for the ring, whose steps merge
 // into one state)
 // Head groups of the all-gather path: K/V travel and are attended group by
 // group, so that group g's attention overlaps the gathers of groups > g.
 static int sp_groups(const ltxb_weights* w) { return w->H % 4 == 0 ? 4 : 1; }
 static int sp_kv_splits(const ltxb_weights* w, const ltxb_config* c) {
-  if (sp_use_ring()) return 1;
+  if (sp_use_ring(w, c)) return 1;
   return attention_kv_splits(c->T, c->T * c->sp_size, w->H / sp_groups(w), 8);
 }
 
@@ -120,9 +150,12 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
   b.n = ws.take<uint8_t>(T * D, act);
   b.qkv = ws.take<uint8_t>(T * 3 * D, act);
   b.ssq = ws.take<float>(T * 32);
+  const bool sp = c->sp_size > 1;
+  const SpAlgo alg = sp_algo(w, c);
+  const bool a2a = sp && alg == SP_ALLTOALL;
   b.q = ws.take<uint8_t>(T * D, act);
-  b.k = ws.take<uint8_t>(Tt * D, act);
-  if (c->sp_size > 1) b.v = ws.take<uint8_t>(Tt * D, act);
+  b.k = ws.take<uint8_t>((a2a ? T : Tt) * D, act);
+  if (sp && !a2a) b.v = ws.take<uint8_t>(Tt * D, act);
   b.gate = ws.take<float>(T * w->G);
   b.o = ws.take<uint8_t>(T * D, act);
   b.x_sa = ws.take<float>(T * D);
@@ -130,19 +163,32 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
   b.kv2 = ws.take<uint8_t>(S * 2 * D, act);
   b.ssq2 = ws.take<float>(S * 32);
   b.k2 = ws.take<uint8_t>(S * D, act);
+  if (w->mode != LTXB_MODE_F32) {
+    b.enc32 = ws.take<float>(S * D);
+    b.enc_split = ws.take<uint8_t>(S * 3 * D, 2);
+    b.kv2_32 = ws.take<float>(S * 2 * D);
+  }
   b.x_ca = ws.take<float>(T * D);
   b.h = ws.take<uint8_t>(T * FF, act);
   if (w->mode == LTXB_MODE_INT8 && !g_fused_dequant) {
-    // the largest int8 matrix expanded at once: the fused q/k/v [3D, D] or an FFN one [FF, D]
-    b.deq = ws.take<uint8_t>(std::max(FF * D, 3 * D * D), 2);
-    b.deq_elems = std::max(FF * D, 3 * D * D);
+    // the largest int8 matrix expanded at once: the fused q/k/v [3D, D], an
+    // FFN one [FF, D], or the prompt K/V's (hi | lo) split [2D, 2D]
+    b.deq_elems = std::max({FF * D, 3 * D * D, 4 * D * D});
+    b.deq = ws.take<uint8_t>(b.deq_elems, 2);
   }
-  if (c->sp_size > 1) {
+  if (sp && !a2a) {
     // split states of one head group (the ring: one state of all heads)
-    const size_t ns = sp_kv_splits(w, c), gh = sp_use_ring() ? w->H : w->H / sp_groups(w);
+    const size_t ns = sp_kv_splits(w, c), gh = alg == SP_RING ? w->H : w->H / sp_groups(w);
     b.o_acc = ws.take<float>(ns * T * gh * 128);
     b.m_st = ws.take<float>(ns * gh * T);
     b.l_st = ws.take<float>(ns * gh * T);
+  }
+  if (a2a) {
+    b.a2a_send = ws.take<uint8_t>(3 * T * D, 2);
+    b.a2a_recv = ws.take<uint8_t>(3 * T * D, 2);
+    b.a2a_o = ws.take<uint8_t>(T * D, 2);
+    b.a2a_orecv = ws.take<uint8_t>(T * D, 2);
+    b.gate_all = ws.take<float>(Tt * w->G);
   }
   return (ws.off + 255) & ~size_t(255);
 }
@@ -316,9 +362,108 @@ static int ring_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, 
 // compute stream runs that group's split-K/V attention as soon as its gather
 // has landed: the gathers of later groups overlap the attention of earlier
 // ones.
+// Head-parallel (all-to-all) variant. Rank r owns heads [r H/N, (r+1) H/N).
+// 1. q, k (this rank's tokens, already normalised and rotated) and v are
+//    regrouped into [x][N][T][D/N] so that the block for rank p is
+//    contiguous; one NCCL group sends block p to rank p and receives rank
+//    p's block for this rank's heads (rank p's tokens are tokens
+//    [p T, (p+1) T), so the received blocks stack into [N T][D/N] in token
+//    order); the gate logits [T, G] are all-gathered in the same group.
+// 2. Attention over all N T queries and keys for this rank's H/N heads
+//    (the single-GPU kernel: no split states, whole waves).
+// 3. A second group returns rows [p T, (p+1) T) of the output to rank p,
+//    and the received [N][T][D/N] blocks are placed into the [T, D]
+//    attention output.
+// The caller's stream waits on the comm stream after each exchange, so the
+// comm stream is idle whenever the caller's stream is.
+// a2a_start enqueues step 1 (the caller's stream only records an event the
+// comm stream waits on); a2a_finish waits for it and runs steps 2-3. Work
+// that needs neither can run on the caller's stream in between.
+static int a2a_start(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* k,
+                     const void* v_local, int ldv_local, const float* gate, cudaStream_t st) {
+  ltxb_comm* cm = c->comm;
+  const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D, Dn = D / N;
+  if ((int)cm->ev.size() < 4) return set_error(LTXB_EINVAL, "sp: communicator event pool too small");
+  const size_t blk = (size_t)T * Dn * 2;  // bytes of one [T][D/N] block
+  uint8_t* send = static_cast<uint8_t*>(b.a2a_send);
+  uint8_t* recv = static_cast<uint8_t*>(b.a2a_recv);
+  const void* srcs[3] = {q, k, v_local};
+  const int lds[3] = {D, D, ldv_local};
+  if (int rc = sp_regroup(srcs, lds, 3, T, D, N, send, st)) return rc;
+  cudaEventRecord(cm->ev[0], st);
+  cudaStreamWaitEvent(cm->comm_stream, cm->ev[0], 0);
+  if (gate) {
+    ncclResult_t gr = ncclAllGather(gate, b.gate_all, (size_t)T * w->G, ncclFloat, cm->nccl, cm->comm_stream);
+    if (gr != ncclSuccess) return set_error(LTXB_ENCCL, "gate all-gather: %s", ncclGetErrorString(gr));
+  }
+  ncclGroupStart();
+  for (int x = 0; x < 3; ++x)
+    for (int p = 0; p < N; ++p) {
+      uint8_t* dst = recv + ((size_t)x * N + p) * blk;
+      const uint8_t* src = send + ((size_t)x * N + p) * blk;
+      if (p == r) continue;
+      ncclSend(src, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+      ncclRecv(dst, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+    }
+  ncclResult_t nr = ncclGroupEnd();
+  if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "q/k/v all-to-all: %s", ncclGetErrorString(nr));
+  for (int x = 0; x < 3; ++x) {  // this rank's own block
+    cudaError_t e = cudaMemcpyAsync(recv + ((size_t)x * N + r) * blk, send + ((size_t)x * N + r) * blk, blk,
+                                    cudaMemcpyDeviceToDevice, cm->comm_stream);
+    if (e != cudaSuccess) return set_cuda_error(e, "sp: local block");
+  }
+  cudaEventRecord(cm->ev[1], cm->comm_stream);
+  return LTXB_OK;
+}
+
+static int a2a_finish(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const float* gate, cudaStream_t st) {
+  ltxb_comm* cm = c->comm;
+  const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D, Dn = D / N, Hn = w->H / N;
+  const size_t blk = (size_t)T * Dn * 2;
+  uint8_t* recv = static_cast<uint8_t*>(b.a2a_recv);
+  cudaStreamWaitEvent(st, cm->ev[1], 0);
+  AttnArgs a{};
+  a.q = recv;
+  a.k = recv + (size_t)N * blk;
+  a.v = recv + 2 * (size_t)N * blk;
+  a.ldq = a.ldk = a.ldv = Dn;
+  a.out = b.a2a_o;
+  a.ldo = Dn;
+  a.gate = gate ? b.gate_all + (size_t)r * Hn : nullptr;
+  a.ldg = w->G;
+  a.Tq = N * T;
+  a.Tkv = N * T;
+  a.H = Hn;
+  a.scale = 0.08838834764831845f;
+  if (int rc = attention_tc(a, st)) return rc;
+  cudaEventRecord(cm->ev[2], st);
+  cudaStreamWaitEvent(cm->comm_stream, cm->ev[2], 0);
+  uint8_t* o = static_cast<uint8_t*>(b.a2a_o);
+  uint8_t* orecv = static_cast<uint8_t*>(b.a2a_orecv);
+  ncclGroupStart();
+  for (int p = 0; p < N; ++p) {
+    if (p == r) continue;
+    ncclSend(o + (size_t)p * blk, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+    ncclRecv(orecv + (size_t)p * blk, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+  }
+  ncclResult_t nr = ncclGroupEnd();
+  if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "attention output all-to-all: %s", ncclGetErrorString(nr));
+  cudaError_t e = cudaMemcpyAsync(orecv + (size_t)r * blk, o + (size_t)r * blk, blk, cudaMemcpyDeviceToDevice,
+                                  cm->comm_stream);
+  if (e != cudaSuccess) return set_cuda_error(e, "sp: local output block");
+  cudaEventRecord(cm->ev[3], cm->comm_stream);
+  cudaStreamWaitEvent(st, cm->ev[3], 0);
+  return sp_ungroup(orecv, T, D, N, b.o, D, st);
+}
+
 static int sp_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* v_local,
                         int ldv_local, const float* gate, cudaStream_t st) {
-  if (sp_use_ring()) return ring_attention(w, c, b, q, v_local, ldv_local, gate, st);
+  const SpAlgo alg = sp_algo(w, c);
+  if (alg == SP_ALLTOALL) {
+    if (int rc = a2a_start(w, c, b, q, b.k, v_local, ldv_local, gate, st)) return rc;
+    return a2a_finish(w, c, b, gate, st);
+  }
+  if (alg == SP_RING) return ring_attention(w, c, b, q, v_local, ldv_local, gate, st);
   ltxb_comm* cm = c->comm;
   const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D;
   const int G = sp_groups(w), Dg = D / G, Hg = w->H / G;
@@ -437,7 +582,10 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   // 4. q/k norm + RoPE (K goes to its slot of the gathered buffer under SP)
   // (the all-gather path regroups K from the attention-output buffer, which
   // is free until the attention writes it)
-  void* k_dst = !sp ? b.k : sp_use_ring() ? col(b.k, (size_t)c->sp_rank * T * D) : b.o;
+  const SpAlgo alg = sp_algo(w, c);
+  void* k_dst = !sp ? b.k
+                : alg == SP_RING ? col(b.k, (size_t)c->sp_rank * T * D)
+                : alg == SP_ALLGATHER ? b.o : b.k;
   {
   Phase p("qk_norm_rope", st);
   if (f32) {
@@ -450,9 +598,70 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
                      T, D, b.q, k_dst, st));
   }
   }
+  // 8. prompt K/V. The 128 text tokens are computed to f32 accuracy in every
+  // mode, as the reference computes them (ltx/block.zig:298-304 with the f32
+  // `lin` and dq4 of :22-26, :462-471): enc in f32, the projection exact to
+  // ~2^-16 on the tensor cores by splitting both operands into bf16 parts
+  // (enc = e_hi + e_lo; an int8 weight q s = w_hi + w_lo exactly, since q s
+  // has at most 15 significant bits): [e_hi | e_hi | e_lo] . [w_hi | w_lo |
+  // w_hi]^T, one GEMM with K = 3D over the expansion (w_hi | w_lo) whose
+  // columns wrap with period 2D (bf16 weights are exact:
+  // [e_hi | e_lo] . [w | w]^T); the k norm in f32; k2 / v2 rounded to bf16
+  // once, as attention operands.
+  auto prompt_kv = [&]() -> int {
+    Phase p("prompt_kv", st);
+    if (f32) {
+      CK(ctx_modulate(io->ctx, S, D, w->psst, io->pts2, nullptr, static_cast<float*>(b.enc), st));
+      CK(run_lin(lc, w->kv2, b.enc, D, S, EPI_F32, b.kv2, 2 * D, b.ssq2, D));
+    } else {
+      const Lin& L = w->kv2;
+      const int parts = L.wq ? 3 : 2;
+      CK(ctx_modulate(io->ctx, S, D, w->psst, io->pts2, nullptr, b.enc32, st));
+      CK(split_f32_bf16(b.enc32, S, D, parts, b.enc_split, st));
+      GemmArgs g{};
+      g.A = b.enc_split;
+      g.lda = parts * D;
+      g.M = S;
+      g.N = 2 * D;
+      g.K = parts * D;
+      g.bn = 128;  // 64 CTAs for the 128 text tokens instead of 32
+      g.epi = EPI_F32;
+      g.bias = L.b;
+      g.out = b.kv2_32;
+      g.ldo = 2 * D;
+      if (L.wq) {
+        if ((size_t)2 * D * 2 * D > b.deq_elems)
+          return set_error(LTXB_EINVAL, "prompt K/V: split expansion exceeds the expansion buffer");
+        g.B = b.deq;
+        g.ldb = 2 * D;
+        g.b_kwrap = 2 * D;
+        CK(gemm_check(g, nullptr));
+        CK(dequant_split(L.wq, L.sc, L.sc_bf16, 2 * D, D, b.deq, st));
+      } else {
+        g.B = L.w;
+        g.ldb = D;
+        g.b_kwrap = D;
+      }
+      CK(gemm_tc(g, st));
+      CK(qk_norm_rope_f32(b.kv2_32, 2 * D, w->kn2, nullptr, nullptr, S, D, nullptr, st, b.k2));
+      CK(cast_rows_f32_bf16(b.kv2_32 + D, 2 * D, col(b.kv2, D), 2 * D, S, D, st));
+    }
+    return LTXB_OK;
+  };
+
   // 5. self-attention
   const float* g1 = gated ? b.gate : nullptr;
-  {
+  if (sp && alg == SP_ALLTOALL) {
+    // the q/k/v exchange runs on the comm stream while the prompt K/V runs here
+    {
+      Phase p("sp_send", st);
+      CK(a2a_start(w, c, b, b.q, b.k, col(b.qkv, 2 * D), 3 * D, g1, st));
+    }
+    CK(prompt_kv());
+    Phase p("attn_self", st);
+    CK(a2a_finish(w, c, b, g1, st));
+  } else {
+    if (sp) CK(prompt_kv());
     Phase p("attn_self", st);
     if (sp)
       CK(sp_attention(w, c, b, b.q, col(b.qkv, 2 * D), 3 * D, g1, st));
@@ -476,13 +685,10 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
     Phase p("norm_ca", st);
     CK(norm_modulate(b.x_sa, T, D, w->sst, io->tstab, io->tidx, c->K, 6, 7, b.n, f32, nullptr, st));
   }
-  // 8. prompt K/V
-  {
-    Phase p("prompt_kv", st);
-    CK(ctx_modulate(io->ctx, S, D, w->psst, io->pts2, f32 ? nullptr : b.enc,
-                    f32 ? static_cast<float*>(b.enc) : nullptr, st));
-    CK(run_lin(lc, w->kv2, b.enc, D, S, f32 ? EPI_F32 : EPI_BF16_SSQ, b.kv2, 2 * D, b.ssq2, D));
-  }
+  // 8. prompt K/V (computed before self-attention under sequence
+  // parallelism, where it overlaps the q/k/v exchange; it reads neither x
+  // nor the attention)
+  if (!sp) CK(prompt_kv());
   // 9. q2 and gate2
   {
     Phase p("gemm_q2", st);
@@ -501,7 +707,6 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
                         static_cast<float*>(b.k2), st));
   } else {
     CK(qk_norm_rope(b.qkv, D, b.ssq, 32, n_ssq, w->qn2, nullptr, nullptr, T, D, b.q, nullptr, st));
-    CK(qk_norm_rope(b.kv2, 2 * D, b.ssq2, 32, n_ssq, w->kn2, nullptr, nullptr, S, D, b.k2, nullptr, st));
   }
   }
   // 11. cross-attention

@@ -87,10 +87,78 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_modulate_kernel(const float*
   }
 }
 
+// The same function with the row held in registers: V float4 per thread
+// (D <= V * 4 * ROW_THREADS), so x is read from HBM once, the sum of squares
+// needs one barrier, and at <= 32 registers a thread eight rows are in flight
+// per SM (the two-pass kernel above is register-limited to four and reads
+// each row twice).
+template <int V>
+__global__ void __launch_bounds__(ROW_THREADS, 8) norm_modulate_reg_kernel(
+    const float* __restrict__ x, int D, const float* __restrict__ sst, const float* __restrict__ tstab,
+    const int* __restrict__ tidx, int tk, int r_shift, int r_scale, void* __restrict__ out, int out_f32) {
+  __shared__ float red[ROW_THREADS / 32];
+  const int t = blockIdx.x;
+  const int nv = D >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * D);
+  float4 v[V];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = threadIdx.x + j * ROW_THREADS;
+    v[j] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    ss = fmaf(v[j].x, v[j].x, ss);
+    ss = fmaf(v[j].y, v[j].y, ss);
+    ss = fmaf(v[j].z, v[j].z, ss);
+    ss = fmaf(v[j].w, v[j].w, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < ROW_THREADS / 32; ++i) ss += red[i];
+  const float r = rsqrtf(ss / (float)D + kEps);
+  const int trow = table_row(tidx, t, tk);
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = threadIdx.x + j * ROW_THREADS;
+    if (i >= nv) break;
+    const int c = i * 4;
+    const float4 sc = ada4(sst, tstab, trow, r_scale, D, c);
+    const float4 sh = ada4(sst, tstab, trow, r_shift, D, c);
+    float4 o;
+    o.x = v[j].x * r * (sc.x + 1.0f) + sh.x;
+    o.y = v[j].y * r * (sc.y + 1.0f) + sh.y;
+    o.z = v[j].z * r * (sc.z + 1.0f) + sh.z;
+    o.w = v[j].w * r * (sc.w + 1.0f) + sh.w;
+    if (out_f32)
+      reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * D)[i] = o;
+    else
+      reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)t * D)[i] =
+          make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
+  }
+}
+
 int norm_modulate(const float* x, int T, int D, const float* sst, const float* tstab, const int* tidx, int tk, int r_shift,
                   int r_scale, void* out, int out_f32, float* rms_copy, cudaStream_t st) {
   if (T <= 0) return LTXB_OK;
   if (D % 4) return set_error(LTXB_EINVAL, "norm_modulate: D %% 4");
+  const int v = (D / 4 + ROW_THREADS - 1) / ROW_THREADS;
+  if (!rms_copy && r_shift >= 0 && v <= 4) {
+    switch (v) {
+      case 1: norm_modulate_reg_kernel<1><<<T, ROW_THREADS, 0, st>>>(x, D, sst, tstab, tidx, tk, r_shift, r_scale, out, out_f32); break;
+      case 2: norm_modulate_reg_kernel<2><<<T, ROW_THREADS, 0, st>>>(x, D, sst, tstab, tidx, tk, r_shift, r_scale, out, out_f32); break;
+      case 3: norm_modulate_reg_kernel<3><<<T, ROW_THREADS, 0, st>>>(x, D, sst, tstab, tidx, tk, r_shift, r_scale, out, out_f32); break;
+      default: norm_modulate_reg_kernel<4><<<T, ROW_THREADS, 0, st>>>(x, D, sst, tstab, tidx, tk, r_shift, r_scale, out, out_f32); break;
+    }
+    launched();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "norm_modulate");
+  }
   norm_modulate_kernel<<<T, ROW_THREADS, 0, st>>>(x, D, sst, tstab, tidx, tk, r_shift, r_scale, out, out_f32, rms_copy);
   launched();
   cudaError_t e = cudaGetLastError();
@@ -227,7 +295,8 @@ __global__ void __launch_bounds__(ROW_THREADS) qk_norm_rope_f32_kernel(const flo
                                                                        const __nv_bfloat16* __restrict__ w,
                                                                        const float* __restrict__ cos,
                                                                        const float* __restrict__ sin, int D,
-                                                                       float* __restrict__ out) {
+                                                                       float* __restrict__ out,
+                                                                       __nv_bfloat16* __restrict__ out_bf16) {
   __shared__ float red[32];
   const int t = blockIdx.x, H = D / 128;
   const float* rr = raw + (size_t)t * ld_raw;
@@ -241,7 +310,6 @@ __global__ void __launch_bounds__(ROW_THREADS) qk_norm_rope_f32_kernel(const flo
   }
   const float ss = block_sum(p, red);
   const float r = rsqrtf(ss / (float)D + kEps);
-  float* o = out + (size_t)t * D;
   for (int u = threadIdx.x; u < H * 64; u += blockDim.x) {
     const int h = u >> 6, i = u & 63;
     const int ca = h * 128 + i, cb = ca + 64;
@@ -253,16 +321,22 @@ __global__ void __launch_bounds__(ROW_THREADS) qk_norm_rope_f32_kernel(const flo
       a = ra;
       b = rb;
     }
-    o[ca] = a;
-    o[cb] = b;
+    if (out) {
+      out[(size_t)t * D + ca] = a;
+      out[(size_t)t * D + cb] = b;
+    } else {
+      out_bf16[(size_t)t * D + ca] = __float2bfloat16_rn(a);
+      out_bf16[(size_t)t * D + cb] = __float2bfloat16_rn(b);
+    }
   }
 }
 
 int qk_norm_rope_f32(const float* raw, int ld_raw, const void* w_bf16, const float* cos, const float* sin, int T,
-                     int D, float* out, cudaStream_t st) {
+                     int D, float* out, cudaStream_t st, void* out_bf16) {
   if (T <= 0) return LTXB_OK;
+  if (!out && !out_bf16) return set_error(LTXB_EINVAL, "qk_norm_rope_f32: no output");
   qk_norm_rope_f32_kernel<<<T, ROW_THREADS, 0, st>>>(raw, ld_raw, reinterpret_cast<const __nv_bfloat16*>(w_bf16),
-                                                     cos, sin, D, out);
+                                                     cos, sin, D, out, reinterpret_cast<__nv_bfloat16*>(out_bf16));
   launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "qk_norm_rope_f32");
@@ -339,6 +413,120 @@ int dequant_weights(const int8_t* q, const void* scales, int scale_bf16, int N, 
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "dequant_weights");
 }
 
+// (w_hi | w_lo) rows from int8 + scales, 8 weights per thread step
+__global__ void dequant_split_kernel(const int8_t* __restrict__ q, const void* __restrict__ scales, int scale_bf16,
+                                     int N, int K, __nv_bfloat16* __restrict__ out) {
+  const size_t n8 = (size_t)N * K / 8;
+  const int G = K / 128;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t e0 = i * 8;
+    const size_t row = e0 / K, col = e0 % K;
+    const int g = (int)(col >> 7);
+    const float s = scale_bf16
+                        ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(scales)[row * G + g] << 16)
+                        : reinterpret_cast<const float*>(scales)[row * G + g];
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(q) + i);
+    const uint32_t w[2] = {v.x, v.y};
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int b = 0; b < 4; b += 2) {
+        const float f0 = (float)(int8_t)((w[j] >> (8 * b)) & 0xFF) * s;
+        const float f1 = (float)(int8_t)((w[j] >> (8 * b + 8)) & 0xFF) * s;
+        const uint32_t h = pack_bf16x2(f0, f1);
+        hi[2 * j + b / 2] = h;
+        lo[2 * j + b / 2] = pack_bf16x2(f0 - bf16_lo(h), f1 - bf16_hi(h));
+      }
+    }
+    __nv_bfloat16* o = out + row * (size_t)(2 * K) + col;
+    *reinterpret_cast<uint4*>(o) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(o + K) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+int dequant_split(const int8_t* q, const void* scales, int scale_bf16, int N, int K, void* out, cudaStream_t st) {
+  if ((size_t)N * K == 0) return LTXB_OK;
+  if (K % 128) return set_error(LTXB_EINVAL, "dequant_split: K %% 128");
+  if ((reinterpret_cast<uintptr_t>(q) & 7) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return set_error(LTXB_EINVAL, "dequant_split: weights 8-byte and output 16-byte aligned");
+  const size_t n8 = (size_t)N * K / 8;
+  int grid = (int)((n8 + 255) / 256);
+  if (grid > 8 * sm_count()) grid = 8 * sm_count();
+  dequant_split_kernel<<<grid, 256, 0, st>>>(q, scales, scale_bf16, N, K, reinterpret_cast<__nv_bfloat16*>(out));
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "dequant_split");
+}
+
+// Head-group regrouping for the sequence-parallel exchange: up to three
+// token-major bf16 matrices [T, D] (row strides ld[x]) -> [x][N][T][D / N]
+// (group p = columns [p D/N, (p + 1) D/N)), and back from [N][T][D / N] to
+// [T, D] (row stride ld_out). 16-byte moves.
+struct RegroupSrc {
+  const __nv_bfloat16* p[3];
+  int ld[3];
+};
+
+__global__ void sp_regroup_kernel(RegroupSrc src, int nsrc, int T, int D, int N, __nv_bfloat16* __restrict__ dst) {
+  const int Dn = D / N, c8 = Dn / 8;
+  const size_t per = (size_t)N * T * c8;
+  const size_t n = (size_t)nsrc * per;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int x = (int)(i / per);
+    const size_t j = i % per;
+    const int p = (int)(j / ((size_t)T * c8));
+    const size_t k = j % ((size_t)T * c8);
+    const int t = (int)(k / c8), c = (int)(k % c8) * 8;
+    const uint4 v = *reinterpret_cast<const uint4*>(src.p[x] + (size_t)t * src.ld[x] + p * Dn + c);
+    *reinterpret_cast<uint4*>(dst + (((size_t)x * N + p) * T + t) * Dn + c) = v;
+  }
+}
+
+__global__ void sp_ungroup_kernel(const __nv_bfloat16* __restrict__ src, int T, int D, int N,
+                                  __nv_bfloat16* __restrict__ out, int ld_out) {
+  const int Dn = D / N, c8 = Dn / 8;
+  const size_t n = (size_t)N * T * c8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int p = (int)(i / ((size_t)T * c8));
+    const size_t k = i % ((size_t)T * c8);
+    const int t = (int)(k / c8), c = (int)(k % c8) * 8;
+    *reinterpret_cast<uint4*>(out + (size_t)t * ld_out + p * Dn + c) =
+        *reinterpret_cast<const uint4*>(src + ((size_t)p * T + t) * Dn + c);
+  }
+}
+
+int sp_regroup(const void* const* srcs, const int* lds, int nsrc, int T, int D, int N, void* dst, cudaStream_t st) {
+  if (nsrc < 1 || nsrc > 3 || N < 1 || D % (8 * N)) return set_error(LTXB_EINVAL, "sp_regroup: D must split into 16-byte groups");
+  RegroupSrc s{};
+  for (int x = 0; x < nsrc; ++x) {
+    s.p[x] = static_cast<const __nv_bfloat16*>(srcs[x]);
+    s.ld[x] = lds[x];
+    if ((reinterpret_cast<uintptr_t>(srcs[x]) & 15) || lds[x] % 8) return set_error(LTXB_EINVAL, "sp_regroup: alignment");
+  }
+  const size_t n = (size_t)nsrc * T * (D / 8);
+  if (n == 0) return LTXB_OK;
+  int grid = (int)((n + 255) / 256);
+  if (grid > 8 * sm_count()) grid = 8 * sm_count();
+  sp_regroup_kernel<<<grid, 256, 0, st>>>(s, nsrc, T, D, N, static_cast<__nv_bfloat16*>(dst));
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "sp_regroup");
+}
+
+int sp_ungroup(const void* src, int T, int D, int N, void* out, int ld_out, cudaStream_t st) {
+  if (N < 1 || D % (8 * N) || ld_out % 8) return set_error(LTXB_EINVAL, "sp_ungroup: D must split into 16-byte groups");
+  const size_t n = (size_t)T * (D / 8);
+  if (n == 0) return LTXB_OK;
+  int grid = (int)((n + 255) / 256);
+  if (grid > 8 * sm_count()) grid = 8 * sm_count();
+  sp_ungroup_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), T, D, N,
+                                          static_cast<__nv_bfloat16*>(out), ld_out);
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "sp_ungroup");
+}
+
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, size_t n) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n / 4; i += (size_t)gridDim.x * blockDim.x) {
     float4 v = reinterpret_cast<const float4*>(in)[i];
@@ -355,6 +543,56 @@ int cast_f32_bf16(const float* in, void* out, size_t n, cudaStream_t st) {
   launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "cast_f32_bf16");
+}
+
+__global__ void split_f32_bf16_kernel(const float* __restrict__ in, int rows, int cols, int parts,
+                                      __nv_bfloat16* __restrict__ out) {
+  const size_t n = (size_t)rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / cols, c = i % cols;
+    const float x = in[i];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+    __nv_bfloat16* o = out + r * (size_t)parts * cols + c;
+    o[0] = hi;
+    if (parts == 2) o[cols] = lo;
+    if (parts == 3) {
+      o[cols] = hi;
+      o[2 * (size_t)cols] = lo;
+    }
+  }
+}
+
+int split_f32_bf16(const float* in, int rows, int cols, int parts, void* out, cudaStream_t st) {
+  const size_t n = (size_t)rows * cols;
+  if (n == 0) return LTXB_OK;
+  if (parts < 2 || parts > 3) return set_error(LTXB_EINVAL, "split_f32_bf16: 2 or 3 parts");
+  int grid = (int)((n + 255) / 256);
+  if (grid > 8 * sm_count()) grid = 8 * sm_count();
+  split_f32_bf16_kernel<<<grid, 256, 0, st>>>(in, rows, cols, parts, reinterpret_cast<__nv_bfloat16*>(out));
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "split_f32_bf16");
+}
+
+__global__ void cast_rows_f32_bf16_kernel(const float* __restrict__ in, int ld_in, __nv_bfloat16* __restrict__ out,
+                                          int ld_out, int rows, int cols) {
+  const size_t n = (size_t)rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / cols, c = i % cols;
+    out[r * ld_out + c] = __float2bfloat16_rn(in[r * ld_in + c]);
+  }
+}
+
+int cast_rows_f32_bf16(const float* in, int ld_in, void* out, int ld_out, int rows, int cols, cudaStream_t st) {
+  const size_t n = (size_t)rows * cols;
+  if (n == 0) return LTXB_OK;
+  int grid = (int)((n + 255) / 256);
+  if (grid > 8 * sm_count()) grid = 8 * sm_count();
+  cast_rows_f32_bf16_kernel<<<grid, 256, 0, st>>>(in, ld_in, reinterpret_cast<__nv_bfloat16*>(out), ld_out, rows, cols);
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "cast_rows_f32_bf16");
 }
 
 __global__ void cast_bf16_f32_kernel(const __nv_bfloat16* __restrict__ in, float* __restrict__ out, size_t n) {

@@ -13,13 +13,26 @@
 namespace ltxb {
 
 // ---------------------------------------------------------------------------
-// GEMM: C[M, N] = A[M, K] . W[N, K]^T, A f32, W bf16. Tile 128 x 128 x 16,
-// 256 threads, 8 x 8 outputs per thread.
+// GEMM: C[M, N] = A[M, K] . W[N, K]^T, A f32, W bf16 or int8 with grouped-128
+// scales (dequantised as the reference's dq4 does, ltx/block.zig:462-471: the
+// int8 value converted to f32 times its group's scale, one f32 multiply).
+// Tile 128 x 128 x 16, 256 threads, 8 x 8 outputs per thread.
 // ---------------------------------------------------------------------------
 constexpr int FB_M = 128, FB_N = 128, FB_K = 16;
 
+__device__ __forceinline__ float w_elem(const __nv_bfloat16* W, const int8_t* wq, const void* scales, int scale_bf16,
+                                        int gn, int k, int K) {
+  if (!wq) return __bfloat162float(W[(size_t)gn * K + k]);
+  const size_t si = (size_t)gn * (K / 128) + (k >> 7);
+  const float sc = scale_bf16 ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(scales)[si] << 16)
+                              : reinterpret_cast<const float*>(scales)[si];
+  return (float)wq[(size_t)gn * K + k] * sc;
+}
+
 __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A, int lda,
-                                                       const __nv_bfloat16* __restrict__ W, int M, int N, int K,
+                                                       const __nv_bfloat16* __restrict__ W,
+                                                       const int8_t* __restrict__ wq, const void* __restrict__ scales,
+                                                       int scale_bf16, int M, int N, int K,
                                                        const __nv_bfloat16* __restrict__ bias, int epi,
                                                        float* __restrict__ out, int ldo, const float* __restrict__ xres,
                                                        const float* __restrict__ sst, const float* __restrict__ tstab,
@@ -42,7 +55,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
       const int r = e >> 4, c = e & 15;
       const int gm = m0 + r, gn = n0 + r;
       sa[c][r] = (gm < M) ? A[(size_t)gm * lda + k0 + c] : 0.f;
-      sw[c][r] = (gn < N) ? __bfloat162float(W[(size_t)gn * K + k0 + c]) : 0.f;
+      sw[c][r] = (gn < N) ? w_elem(W, wq, scales, scale_bf16, gn, k0 + c, K) : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -90,11 +103,15 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
 
 int gemm_f32(const float* A, int lda, const void* W, int M, int N, int K, const void* bias, int epi, float* out,
              int ldo, float* /*ssq*/, int /*ssq_ld*/, const float* xres, const float* sst, const float* tstab,
-             const int* tidx, int tk, int ada_row, cudaStream_t st) {
+             const int* tidx, int tk, int ada_row, cudaStream_t st, const int8_t* wq, const void* scales,
+             int scale_bf16) {
   if (M <= 0 || N <= 0) return LTXB_OK;
   if (K % FB_K) return set_error(LTXB_EINVAL, "gemm_f32: K %% 16");
+  if (wq && (K % 128 || !scales)) return set_error(LTXB_EINVAL, "gemm_f32: int8 weights need K %% 128 and scales");
+  if (!wq && !W) return set_error(LTXB_EINVAL, "gemm_f32: no weights");
   dim3 grid((N + FB_N - 1) / FB_N, (M + FB_M - 1) / FB_M);
-  gemm_f32_kernel<<<grid, 256, 0, st>>>(A, lda, reinterpret_cast<const __nv_bfloat16*>(W), M, N, K,
+  gemm_f32_kernel<<<grid, 256, 0, st>>>(A, lda, reinterpret_cast<const __nv_bfloat16*>(W), wq, scales, scale_bf16, M,
+                                        N, K,
                                         reinterpret_cast<const __nv_bfloat16*>(bias), epi, out, ldo, xres, sst, tstab,
                                         tidx, tk, ada_row);
   launched();

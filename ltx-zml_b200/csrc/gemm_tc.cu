@@ -27,20 +27,25 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_GROUP_M = 16;  // M tiles walked together for L2 reuse
 
-template <int BN, bool BQ8>
+// XBUF: the gated-residual epilogue's two [128 x 32] f32 chunk buffers (the
+// residual input arrives there by TMA, the output leaves by TMA store).
+template <int BN, bool BQ8, bool XBUF = false>
 struct GemmCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;   // 16 KB
   static constexpr int B_BYTES = BN * GEMM_BK * 2;        // bf16 tile
   static constexpr int BQ_BYTES = BQ8 ? BN * GEMM_BK : 0; // int8 tile
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + BQ_BYTES;
-  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int XCHUNK = GEMM_BM * 32 * 4;         // 16 KB
+  static constexpr int XBUF_BYTES = XBUF ? 2 * XCHUNK : 0;
+  static constexpr int STAGES_RAW = ((XBUF ? 192 : 200) * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int NUM_THREADS = BQ8 ? 320 : 192;
   static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
-  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 4 + 2) + 16;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + XBUF_BYTES + BAR_BYTES;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns must be a power of two");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
 __device__ __forceinline__ float gelu_tanh_f(float x) {
@@ -77,6 +82,7 @@ __device__ __forceinline__ uint4 dequant8(uint2 q, float s) {
     f[i] = (__uint_as_float(b0) - bias) * s;
     f[4 + i] = (__uint_as_float(b1) - bias) * s;
   }
+
   uint4 o;
   o.x = pack_bf16x2(f[0], f[1]);
   o.y = pack_bf16x2(f[2], f[3]);
@@ -88,26 +94,31 @@ __device__ __forceinline__ uint4 dequant8(uint2 q, float s) {
 template <int BN, bool BQ8, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmO,
                    const GemmArgs args) {
-  using C = GemmCfg<BN, BQ8>;
+  constexpr bool XB = EPI == EPI_RESID_F32;
+  using C = GemmCfg<BN, BQ8, XB>;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + S * C::A_BYTES;
   uint8_t* sBq = sB + S * C::B_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sBq + S * C::BQ_BYTES);
+  uint8_t* xbuf = sBq + S * C::BQ_BYTES;  // [2][128 rows][128 B], 128B-swizzled (XB only)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xbuf + C::XBUF_BYTES);
   uint64_t* full = bars;            // TMA -> (dequant | MMA)
   uint64_t* deq = bars + S;         // dequant -> MMA
   uint64_t* empty = bars + 2 * S;   // MMA -> TMA
   uint64_t* tfull = bars + 3 * S;   // MMA -> epilogue, 2 accumulators
   uint64_t* tempty = tfull + 2;     // epilogue -> MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* xfull = tempty + 2;     // residual chunk landed (XB), 2 buffers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 2);
 
   const int warp = warp_id(), lane = lane_id();
   const int M = args.M, N = args.N, K = args.K;
   const int num_m = (M + GEMM_BM - 1) / GEMM_BM, num_n = N / BN, nkb = K / GEMM_BK;
   const int num_tiles = num_m * num_n;
+  const int kw = args.b_kwrap > 0 ? args.b_kwrap : K;  // B's own K (columns repeat with this period)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -118,12 +129,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 4);
+      mbar_init(&xfull[i], 1);
     }
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (XB && args.xres) {
+      prefetch_tmap(&tmX);
+      prefetch_tmap(&tmO);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
@@ -144,10 +160,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
           if (!mbar_wait(&empty[s], ph ^ 1, 0x101)) goto done;
           mbar_arrive_expect_tx(&full[s], bytes);
           tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * GEMM_BK, m * GEMM_BM);
+          const int bx = (kb * GEMM_BK) % kw;
           if (BQ8)
-            tma_load_2d(sBq + s * C::BQ_BYTES, &tmB, &full[s], kb * GEMM_BK, n * BN);
+            tma_load_2d(sBq + s * C::BQ_BYTES, &tmB, &full[s], bx, n * BN);
           else
-            tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * GEMM_BK, n * BN);
+            tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], bx, n * BN);
           if (++s == S) { s = 0; ph ^= 1; }
         }
       }
@@ -178,6 +195,107 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
         }
         umma_commit(&tfull[acc]);
       }
+    }
+  } else if (warp < 6 && XB && args.xres != nullptr) {
+    // ---------------- gated-residual epilogue through shared memory ----------------
+    // out = xres + y * ada, 32 columns at a time: the [128 x 32] f32 chunk of
+    // xres arrives by TMA one chunk ahead, each thread (one row) combines it
+    // with its accumulator row in place, and one TMA store writes the chunk
+    // back as whole rows. Thread 64 (warp 2, lane 0) issues the copies; two
+    // buffers alternate, a buffer is reloaded only once the store that last
+    // read it is done reading (wait_group.read), and all 128 threads pass
+    // every named barrier together (failures are OR-reduced across them).
+    const int q = warp & 3;
+    const int row_local = q * 32 + lane;
+    const bool leader = threadIdx.x == 64;
+    constexpr int NCH = BN / 32;
+    uint32_t issued = 0, g = 0;  // residual chunks requested / consumed
+    auto load_chunk = [&](int tile, int cc) {
+      int m, n;
+      tile_coords(tile, num_m, num_n, m, n);
+      const int b = issued & 1;
+      mbar_arrive_expect_tx(&xfull[b], C::XCHUNK);
+      tma_load_2d(xbuf + b * C::XCHUNK, &tmX, &xfull[b], n * BN + cc * 32, m * GEMM_BM);
+      ++issued;
+    };
+    if (leader && (int)blockIdx.x < num_tiles) load_chunk(blockIdx.x, 0);
+    int it = 0;
+    bool failed = false;
+    for (int tile = blockIdx.x; tile < num_tiles && !failed; tile += gridDim.x, ++it) {
+      int m, n;
+      tile_coords(tile, num_m, num_n, m, n);
+      const int acc = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      const bool tok = warp_wait(&tfull[acc], aph, 0x104);
+      if (named_bar_any(1, 128, !tok)) break;
+      tc_fence_after();
+      const int row = m * GEMM_BM + row_local;
+      const int trow = row < M ? table_row(args.tidx, row, args.tk) : 0;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int cc = 0; cc < NCH; ++cc, ++g) {
+        uint32_t r[32];
+        tmem_ld32(tbase + cc * 32, r);
+        tmem_wait_ld();
+        const int col0 = n * BN + cc * 32;
+        const int b = g & 1;
+        const bool ok = warp_wait(&xfull[b], (g >> 1) & 1, 0x106);
+        if (ok) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (args.bias != nullptr) {
+            const uint4* bp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(args.bias) + col0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 bb = __ldg(bp + j);
+              v[8 * j + 0] += bf16_lo(bb.x); v[8 * j + 1] += bf16_hi(bb.x);
+              v[8 * j + 2] += bf16_lo(bb.y); v[8 * j + 3] += bf16_hi(bb.y);
+              v[8 * j + 4] += bf16_lo(bb.z); v[8 * j + 5] += bf16_hi(bb.z);
+              v[8 * j + 6] += bf16_lo(bb.w); v[8 * j + 7] += bf16_hi(bb.w);
+            }
+          }
+          const float4* sp = reinterpret_cast<const float4*>(args.sst + (size_t)args.ada_row * args.ada_d + col0);
+          const float4* tp = reinterpret_cast<const float4*>(
+              args.tstab + ((size_t)trow * 9 + args.ada_row) * args.ada_d + col0);
+          uint8_t* rowp = xbuf + b * C::XCHUNK + row_local * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4* slot = reinterpret_cast<float4*>(rowp + ((j ^ (row_local & 7)) << 4));
+            const float4 xv = *slot, sv = __ldg(sp + j), tv = __ldg(tp + j);
+            float4 o;
+            o.x = xv.x + v[4 * j + 0] * (tv.x + sv.x);
+            o.y = xv.y + v[4 * j + 1] * (tv.y + sv.y);
+            o.z = xv.z + v[4 * j + 2] * (tv.z + sv.z);
+            o.w = xv.w + v[4 * j + 3] * (tv.w + sv.w);
+            *slot = o;
+          }
+          fence_proxy_async_smem();
+        }
+        if (named_bar_any(1, 128, !ok)) {
+          failed = true;
+          break;
+        }
+        if (leader) {
+          tma_store_2d(&tmO, xbuf + b * C::XCHUNK, col0, m * GEMM_BM);
+          bulk_commit();
+          const int ntile = cc + 1 < NCH ? tile : tile + (int)gridDim.x;
+          if (ntile < num_tiles) {
+            bulk_wait_read<1>();  // the store that last read the other buffer is done with it
+            load_chunk(ntile, cc + 1 < NCH ? cc + 1 : 0);
+          }
+        }
+      }
+      if (failed) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (leader) {
+      bulk_wait_all();
+      // a residual chunk requested but never consumed (only after a failed
+      // wait): let it land before the CTA's shared memory is released
+      if (issued > g) mbar_wait(&xfull[(issued - 1) & 1], ((issued - 1) >> 1) & 1, 0x107);
     }
   } else if (warp < 6) {
     // ---------------- epilogue ----------------
@@ -281,7 +399,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
     const int td = threadIdx.x - 192;  // 0..127
     int s = 0;
     uint32_t ph = 0;
-    const int ngroups = K / 128;
+    const int ngroups = kw / 128;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int m, n;
       tile_coords(tile, num_m, num_n, m, n);
@@ -289,7 +407,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
         if (!warp_wait(&full[s], ph, 0x105)) goto done;
         const uint8_t* src = sBq + s * C::BQ_BYTES;
         uint8_t* dst = sB + s * C::B_BYTES;
-        const int g = (kb * GEMM_BK) >> 7;
+        const int g = ((kb * GEMM_BK) % kw) >> 7;
 #pragma unroll 4
         for (int j = 0; j < BN * 8 / 128; ++j) {
           const int id = j * 128 + td;
@@ -322,8 +440,9 @@ done:
 // ---------------------------------------------------------------------------
 
 template <int BN, bool BQ8, int EPI>
-static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
-  using C = GemmCfg<BN, BQ8>;
+static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx, const CUtensorMap& to,
+                      const GemmArgs& a, cudaStream_t st) {
+  using C = GemmCfg<BN, BQ8, EPI == EPI_RESID_F32>;
   auto kern = gemm_tc_kernel<BN, BQ8, EPI>;
   // per device and instance: the shared-memory opt-in, set once (host threads
   // may race to set it; the call is idempotent and the flag is atomic)
@@ -338,7 +457,7 @@ static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
   }
   const int num_tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * (a.N / BN);
   const int grid = num_tiles < sm_count() ? num_tiles : sm_count();
-  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, a);
+  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tx, to, a);
   launched();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "gemm launch");
@@ -346,14 +465,15 @@ static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
 }
 
 template <int BN, bool BQ8>
-static int dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+static int dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx, const CUtensorMap& to,
+                        const GemmArgs& a, cudaStream_t st) {
   switch (a.epi) {
-    case EPI_BF16: return launch_one<BN, BQ8, EPI_BF16>(ta, tb, a, st);
-    case EPI_BF16_SSQ: return launch_one<BN, BQ8, EPI_BF16_SSQ>(ta, tb, a, st);
-    case EPI_GELU_BF16: return launch_one<BN, BQ8, EPI_GELU_BF16>(ta, tb, a, st);
-    case EPI_RESID_F32: return launch_one<BN, BQ8, EPI_RESID_F32>(ta, tb, a, st);
-    case EPI_GATE2SIG_F32: return launch_one<BN, BQ8, EPI_GATE2SIG_F32>(ta, tb, a, st);
-    case EPI_F32: return launch_one<BN, BQ8, EPI_F32>(ta, tb, a, st);
+    case EPI_BF16: return launch_one<BN, BQ8, EPI_BF16>(ta, tb, tx, to, a, st);
+    case EPI_BF16_SSQ: return launch_one<BN, BQ8, EPI_BF16_SSQ>(ta, tb, tx, to, a, st);
+    case EPI_GELU_BF16: return launch_one<BN, BQ8, EPI_GELU_BF16>(ta, tb, tx, to, a, st);
+    case EPI_RESID_F32: return launch_one<BN, BQ8, EPI_RESID_F32>(ta, tb, tx, to, a, st);
+    case EPI_GATE2SIG_F32: return launch_one<BN, BQ8, EPI_GATE2SIG_F32>(ta, tb, tx, to, a, st);
+    case EPI_F32: return launch_one<BN, BQ8, EPI_F32>(ta, tb, tx, to, a, st);
   }
   return set_error(LTXB_EINVAL, "gemm: unknown epilogue");
 }
@@ -366,6 +486,9 @@ int gemm_check(const GemmArgs& a, int* bn_out) {
   if (bn == 0) bn = (a.N % 256 == 0) ? 256 : (a.N % 128 == 0) ? 128 : (a.N % 32 == 0 ? 32 : 0);
   if (bn == 0 || a.N % bn) return set_error(LTXB_EINVAL, "gemm: N must be a multiple of 32");
   if (a.b_int8 && bn == 32) return set_error(LTXB_EINVAL, "gemm: int8 weights need N % 128 == 0");
+  // a K block of 64 (int8: a scale group of 128) never straddles B's column period
+  if (a.b_kwrap < 0 || (a.b_kwrap > 0 && a.b_kwrap % (a.b_int8 ? 128 : GEMM_BK)))
+    return set_error(LTXB_EINVAL, "gemm: B's column period must be whole 64 (int8: 128) column blocks");
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15) || (a.lda % 8) ||
       (a.ldb % (a.b_int8 ? 16 : 8)) || (a.ldo % 8))
     return set_error(LTXB_EINVAL, "gemm: operands must be 16-byte aligned with 16-byte row strides");
@@ -384,20 +507,32 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st) {
   int rc = make_tmap_2d(&ta, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda, GEMM_BK, GEMM_BM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  const int kw = a.b_kwrap > 0 ? a.b_kwrap : a.K;
   if (a.b_int8)
-    rc = make_tmap_2d(&tb, a.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, a.ldb, GEMM_BK, bn,
+    rc = make_tmap_2d(&tb, a.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, kw, a.N, a.ldb, GEMM_BK, bn,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
   else
-    rc = make_tmap_2d(&tb, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, a.ldb, GEMM_BK, bn,
+    rc = make_tmap_2d(&tb, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kw, a.N, a.ldb, GEMM_BK, bn,
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if (a.b_int8) {
-    if (bn == 256) return dispatch_epi<256, true>(ta, tb, a, st);
-    return dispatch_epi<128, true>(ta, tb, a, st);
+  // the gated-residual epilogue moves [128 x 32] f32 chunks of the residual
+  // input and the output by TMA (128-byte rows, 128B swizzle)
+  CUtensorMap tx = ta, to = ta;
+  if (a.epi == EPI_RESID_F32 && a.xres) {
+    rc = make_tmap_2d(&tx, a.xres, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.N, a.M, a.ldx, 32, GEMM_BM,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc)
+      rc = make_tmap_2d(&to, a.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.N, a.M, a.ldo, 32, GEMM_BM,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
   }
-  if (bn == 256) return dispatch_epi<256, false>(ta, tb, a, st);
-  if (bn == 128) return dispatch_epi<128, false>(ta, tb, a, st);
-  return dispatch_epi<32, false>(ta, tb, a, st);
+  if (a.b_int8) {
+    if (bn == 256) return dispatch_epi<256, true>(ta, tb, tx, to, a, st);
+    return dispatch_epi<128, true>(ta, tb, tx, to, a, st);
+  }
+  if (bn == 256) return dispatch_epi<256, false>(ta, tb, tx, to, a, st);
+  if (bn == 128) return dispatch_epi<128, false>(ta, tb, tx, to, a, st);
+  return dispatch_epi<32, false>(ta, tb, tx, to, a, st);
 }
 
 }  // namespace ltxb

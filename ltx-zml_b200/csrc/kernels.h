@@ -76,6 +76,9 @@ struct GemmArgs {
   int tk;              // rows of tstab
   int ada_row;
   int ada_d;
+  // split-precision products (the f32-exact prompt K/V): B's columns repeat
+  // with period b_kwrap (its real K; 0 = no repeat)
+  int b_kwrap;
 };
 // Shape, alignment and tile checks of gemm_tc, on the host, launching
 // nothing; *bn_out receives the N tile gemm_tc will use.
@@ -143,16 +146,33 @@ int qk_norm_rope2(const void* raw_q, const void* raw_k, int ld_raw, const float*
                   int D, void* out_q, void* out_k, cudaStream_t st);
 
 // ---- f32 SIMT path (LTXB_MODE_F32) ----
-// C[M, N] = A[M, K] (f32) . W[N, K]^T (bf16 upcast) + bias, epilogues as Epi
+// C[M, N] = A[M, K] (f32) . W[N, K]^T + bias, epilogues as Epi; W bf16
+// (upcast) or, with wq set, int8 [N, K] times grouped-128 scales in f32
 int gemm_f32(const float* A, int lda, const void* W, int M, int N, int K, const void* bias, int epi, float* out,
              int ldo, float* ssq, int ssq_ld, const float* xres, const float* sst, const float* tstab,
-             const int* tidx, int tk, int ada_row, cudaStream_t st);
+             const int* tidx, int tk, int ada_row, cudaStream_t st, const int8_t* wq = nullptr,
+             const void* scales = nullptr, int scale_bf16 = 0);
 // f32 attention: q/k/v f32 [T, H, 128] (row strides ld*) -> out f32 [Tq, H*128],
 // with optional gate [Tq, ldg]
 int attention_f32(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* out,
                   const float* gate, int ldg, int Tq, int Tkv, int H, float scale, cudaStream_t st);
-// q/k norm (+RoPE) on f32 raw projections (ssq computed in-kernel)
+// q/k norm (+RoPE) on f32 raw projections (ssq computed in-kernel); f32
+// output, or bf16 (one rounding) into out_bf16 when out is null
 int qk_norm_rope_f32(const float* raw, int ld_raw, const void* w_bf16, const float* cos, const float* sin, int T,
-                     int D, float* out, cudaStream_t st);
+                     int D, float* out, cudaStream_t st, void* out_bf16 = nullptr);
+// x f32 [rows, cols] -> [rows, parts * cols] bf16: parts 2 = (hi | lo),
+// parts 3 = (hi | hi | lo), with hi = bf16(x), lo = bf16(x - hi), so that
+// x = hi + lo to ~2^-16
+int split_f32_bf16(const float* in, int rows, int cols, int parts, void* out, cudaStream_t st);
+// int8 [N, K] + grouped-128 scales -> bf16 [N, 2K] = (w_hi | w_lo) with
+// w_hi = bf16(q s) and w_lo = bf16(q s - w_hi): q s has at most 15
+// significant bits (bf16 scales), so w_hi + w_lo = q s exactly
+int dequant_split(const int8_t* q, const void* scales, int scale_bf16, int N, int K, void* out, cudaStream_t st);
+// sequence-parallel head-group layout: nsrc (<= 3) bf16 [T, D] matrices with
+// row strides lds -> dst [nsrc][N][T][D/N]; and [N][T][D/N] -> out [T, D]
+int sp_regroup(const void* const* srcs, const int* lds, int nsrc, int T, int D, int N, void* dst, cudaStream_t st);
+int sp_ungroup(const void* src, int T, int D, int N, void* out, int ld_out, cudaStream_t st);
+// rows x cols f32 (row stride ld_in) -> bf16 (row stride ld_out)
+int cast_rows_f32_bf16(const float* in, int ld_in, void* out, int ld_out, int rows, int cols, cudaStream_t st);
 
 }  // namespace ltxb

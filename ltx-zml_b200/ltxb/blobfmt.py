@@ -105,3 +105,40 @@ def write_dir(directory, tensors, block: int = 0, provenance: dict | None = None
     (d / "blob.bin").write_bytes(blob)
     (d / "blob_manifest.json").write_text(json.dumps(man, indent=1))
     return man
+
+
+def synthetic_block(device, d: int = 4096, ff: int = 16384, seed: int = 0, block: int = 0, q8=Q8_EXT,
+                    outlier_frac: float = 0.005, outlier_mult: float = 20.0):
+    """A seeded synthetic block in this format:
+    weights N(0, 0.02) drawn on `device` (norm weights 1 + N(0, 0.02), the
+    two modulation tables f32); every weight in `q8` gets 0.5% of its input
+    channels scaled x20, then symmetric int8 grouped-128 quantisation with
+    scale = absmax / 127 rounded to bf16 (q from the rounded scale), stored
+    as `::q8` / `::q8scale` only. Returns (blob bytes, entries)."""
+    import torch
+    g = torch.Generator(device=device)
+    tensors = []
+    for i, (suffix, spec, dt) in enumerate(BLOCK_TENSORS):
+        shape = shape_of(spec, d, ff)
+        g.manual_seed(seed * 1000 + i)
+        w = torch.randn(*shape, generator=g, device=device) * 0.02
+        name = f"transformer_blocks.{block}.{suffix}"
+        if dt == "F32":
+            tensors.append((name, "F32", shape, w.cpu().numpy().tobytes()))
+            continue
+        if "norm" in suffix:
+            w = w + 1.0
+        if suffix in q8:
+            k = shape[1]
+            cols = torch.randperm(k, generator=g, device=device)[: max(1, round(outlier_frac * k))]
+            w[:, cols] *= outlier_mult
+            wg = w.view(shape[0], k // 128, 128)
+            amax = wg.abs().amax(-1, keepdim=True)
+            sc = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax)).to(torch.bfloat16)
+            q = torch.clamp(torch.round(wg / sc.float()), -128, 127).to(torch.int8).view(shape)
+            tensors.append((name + "::q8", "I8", shape, q.cpu().numpy().tobytes()))
+            tensors.append((name + "::q8scale", "BF16", [shape[0], k // 128],
+                            sc.view(torch.int16).view(shape[0], k // 128).cpu().numpy().tobytes()))
+        else:
+            tensors.append((name, "BF16", shape, w.to(torch.bfloat16).view(torch.int16).cpu().numpy().tobytes()))
+    return pack(tensors)

@@ -4,6 +4,12 @@ timing and for sizing profiler captures:
     PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench attention --T 8192 --H 8 --reps 3
     PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench dq_gemm --M 8192 --N 4096 --K 4096 [--unfused]
     PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench gemm --M 8192 --N 4096 --K 4096
+    PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench block --T 8192 --reps 3
+
+`block` runs whole int8 blocks (BASELINE config-3 architecture: D 4096,
+32 x 128 heads, FFN 16384, S 128, int8 g128 EXT weights with bf16 scales)
+at T tokens, so every kernel of the block can be captured at a size chosen
+for the profiler (`ncu -k regex:<kernel> -s <skip> -c 1`).
 
 Inputs are seeded N(0, 1) activations and N(0, 0.02) weights generated on the
 device; each run prints one line with the CUDA-event time per launch and the
@@ -33,7 +39,7 @@ def _time(fn, reps: int) -> float:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=("attention", "dq_gemm", "gemm"))
+    ap.add_argument("op", choices=("attention", "dq_gemm", "gemm", "block"))
     ap.add_argument("--T", type=int, default=8192)
     ap.add_argument("--Tkv", type=int, default=0)
     ap.add_argument("--H", type=int, default=8)
@@ -45,6 +51,26 @@ def main(argv=None) -> int:
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(0)
+    if a.op == "block":
+        from . import QBlock, QSET_EXT, Blob, build_quant_bufs, blobfmt
+        data, ent = blobfmt.synthetic_block(dev, 4096, 16384)
+        w = build_quant_bufs(Blob.from_bytes(data, ent), 0, qset=QSET_EXT, hidden=4096, ff=16384)
+        del data
+        x = torch.randn(a.T, 4096, generator=g, device=dev)
+        tstab = torch.randn(1, 9, 4096, generator=g, device=dev) * 0.1
+        tidx = torch.zeros(a.T, dtype=torch.int32, device=dev)
+        ctx = torch.randn(128, 4096, generator=g, device=dev)
+        pts2 = torch.randn(2, 4096, generator=g, device=dev) * 0.1
+        ang = torch.rand(a.T, 32, 64, generator=g, device=dev) * 6.283185307179586
+        cos, sin = torch.cos(ang), torch.sin(ang)
+        out = torch.empty_like(x)
+        blk = QBlock(w)
+        ms = _time(lambda: blk.forward(x, tstab, tidx, ctx, pts2, cos, sin, out=out), a.reps)
+        T, D, S, FF = a.T, 4096, 128, 16384
+        flop = 12 * T * D * D + 4 * S * D * D + 4 * T * D * 32 + 4 * T * D * FF + 4 * T * T * D + 4 * T * S * D
+        print(f"block T={a.T}: {ms:.4f} ms/block {flop / ms / 1e9:.1f} TFLOP/s status={device_status()}")
+        w.free()
+        return 0
     if a.op == "attention":
         tkv = a.Tkv or a.T
         q = torch.randn(a.T, a.H, 128, generator=g, device=dev).to(torch.bfloat16)

@@ -1,5 +1,6 @@
-"""Multi-GPU test of the sequence-parallel block (K/V all-gather + split-K/V
-attention by default, the send/recv ring with LTXB_SP_RING=1, over NCCL):
+"""Multi-GPU test of the sequence-parallel block over NCCL, with each of the
+library's exchanges (LTXB_SP): the head-parallel all-to-all (the default),
+the K/V all-gather with split-K/V attention, and the send/recv ring:
 tokens split across ranks, each rank holding its slice of x / tidx / RoPE
 tables; the gathered outputs must match the f64 oracle of the whole block and
 the single-GPU run of the library. Needs >= 2 GPUs (skipped otherwise).
@@ -23,7 +24,8 @@ D, FF, S = 256, 512, 16
 
 def _worker(rank, world, uid, grid, seed, mode, algo, q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    os.environ["LTXB_SP_RING"] = "1" if algo == "ring" else "0"
+    os.environ["LTXB_SP"] = algo
+    os.environ["LTXB_SP_RING"] = "0"
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "ltx-zml_b200"), os.path.join(root, "tests")]
@@ -59,7 +61,7 @@ def _worker(rank, world, uid, grid, seed, mode, algo, q):
         q.put((rank, None, False, -99, repr(exc)))
 
 
-def _run(world, grid, seed, mode, algo="allgather"):
+def _run(world, grid, seed, mode, algo="alltoall"):
     return _spawn(world, _worker, (grid, seed, mode, algo))
 
 
@@ -90,7 +92,7 @@ def _spawn(world, target, args):
     return np.concatenate([res[r][0] for r in range(world)], axis=0)
 
 
-@pytest.mark.parametrize("algo", ["allgather", "ring"])
+@pytest.mark.parametrize("algo", ["alltoall", "allgather", "ring"])
 @pytest.mark.parametrize("mode,grid", [("bf16", (2, 4, 32)), ("int8", (3, 4, 16))])
 def test_sp_block_matches_single_gpu_and_oracle(mode, grid, algo):
     if torch.cuda.device_count() < 2:

@@ -214,3 +214,65 @@ def test_rank_failure_surfaces_as_an_error_gloo():
             p.terminate()
     assert res[1] == "raised"
     assert res[0].startswith("error after"), res[0]
+
+
+# ---------------------------------------------------------------------------
+# the head-parallel exchange: q/k/v to the ranks owning their heads
+# ---------------------------------------------------------------------------
+
+def _alltoall_worker(rank, world, port, T, H, seed, result_q):
+    """The block's SP_ALLTOALL arithmetic with real ranks: q/k/v [T, H, 128]
+    of this rank's tokens are regrouped into [N][T][H/N, 128] (block p holds
+    rank p's heads), one round of point-to-point messages sends block p to
+    rank p and receives rank p's tokens for this rank's heads, which stack
+    into [N T][H/N, 128] in global token order; attention over all tokens for
+    the owned heads; the output rows [p T, (p+1) T) go back to rank p, whose
+    received blocks are placed at head group p of its [T, H, 128] output."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(seed)
+        full = [torch.randn(world * T, H, 128, generator=g, dtype=torch.float64) for _ in range(3)]
+        sl = slice(rank * T, (rank + 1) * T)
+        hn = H // world
+
+        def exchange(blocks):  # blocks[p] goes to rank p; returns what each rank p sent here
+            out = [None] * world
+            reqs = []
+            for p in range(world):
+                if p == rank:
+                    out[p] = blocks[p].clone()
+                    continue
+                out[p] = torch.empty(blocks[p].shape, dtype=blocks[p].dtype)
+                reqs += [dist.isend(blocks[p].contiguous(), p), dist.irecv(out[p], p)]
+            for r_ in reqs:
+                r_.wait()
+            return out
+
+        mine = [x[sl] for x in full]  # this rank's tokens, every head
+        recv = [exchange([x[:, p * hn:(p + 1) * hn] for p in range(world)]) for x in mine]
+        q, k, v = (torch.cat(blocks, dim=0) for blocks in recv)  # [N T, H/N, 128]
+        o = ref.sdpa_dense(q, k, v)  # this rank's heads, all tokens
+        back = exchange([o[p * T:(p + 1) * T] for p in range(world)])
+        got = torch.cat(back, dim=1)  # [T, H, 128]: head group p from rank p
+        want = ref.sdpa_dense(full[0][sl], full[1], full[2])
+        result_q.put((rank, ref.rel_rms(got.numpy(), want.numpy())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,T,H", [(2, 40, 2), (3, 24, 6)])
+def test_alltoall_head_parallel_attention_gloo(world, T, H):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_alltoall_worker, args=(r, world, port, T, H, 13, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err in res:
+        assert err < 1e-12, (rank, err)
