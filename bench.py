@@ -275,6 +275,116 @@ def run_reference(args, rank: int, world: int):
 
 
 # ---------------------------------------------------------------------------
+# host placement: each rank's pinned buffers on its GPU's NUMA node
+# ---------------------------------------------------------------------------
+
+def _parse_cpulist(text: str) -> set:
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.update(range(int(a), int(b) + 1))
+        else:
+            cpus.add(int(part))
+    return cpus
+
+
+def gpu_host_locality(local_rank: int) -> dict:
+    """The GPU's PCI address, NUMA node and local CPUs as sysfs reports them."""
+    info = {"pci": None, "numa_node": None, "local_cpus": None}
+    try:
+        pr = torch.cuda.get_device_properties(local_rank)
+        pci = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        info["pci"] = pci
+        d = pathlib.Path("/sys/bus/pci/devices") / pci
+        if (d / "numa_node").exists():
+            info["numa_node"] = int((d / "numa_node").read_text())
+        if (d / "local_cpulist").exists():
+            info["local_cpus"] = (d / "local_cpulist").read_text().strip()
+    except Exception:
+        pass
+    return info
+
+
+def bind_to_gpu_numa(local_rank: int) -> dict:
+    """Restricts this process to the GPU's local CPUs (when sysfs names a
+    proper subset), so pinned host buffers allocated afterwards land on the
+    GPU's NUMA node (pages are placed where they are first touched)."""
+    info = gpu_host_locality(local_rank)
+    info["bound"] = False
+    try:
+        allowed = os.sched_getaffinity(0)
+        if info["local_cpus"]:
+            cpus = _parse_cpulist(info["local_cpus"]) & allowed
+            if cpus and cpus != allowed:
+                os.sched_setaffinity(0, cpus)
+                info["bound"] = True
+        info["cpus_allowed"] = len(os.sched_getaffinity(0))
+    except Exception:
+        pass
+    return info
+
+
+def run_copy(args, rank: int, world: int, local_rank: int):
+    """Host copies alone: every step copies this rank's x slice (T/N x D f32)
+    from pinned host memory to the GPU and a block-output-sized buffer back,
+    on two streams at once (the host pipe's steady state), with no compute.
+    Prints the aggregate bytes per second over all ranks (max-over-ranks
+    time), the bound the end-to-end number cannot beat."""
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    loc = bind_to_gpu_numa(local_rank) if not args.no_numa_bind else gpu_host_locality(local_rank)
+    T = T_TOTAL // world
+    x_host = torch.randn(T, D).pin_memory()
+    out_host = torch.empty(T, D).pin_memory()
+    x_dev = torch.empty(T, D, device=dev)
+    out_dev = torch.randn(T, D, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def step():
+        with torch.cuda.stream(s_in):
+            x_dev.copy_(x_host, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            out_host.copy_(out_dev, non_blocking=True)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    locs = [loc]
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        locs = [None] * world
+        dist.all_gather_object(locs, loc)
+    if rank == 0:
+        nbytes = 2 * T * D * 4 * world
+        print(json.dumps({"metric": "host_copy_aggregate_gbs", "value": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                          "unit": "GB/s", "n_gpus": world, "steps": args.steps, "ms_per_step": round(ms, 3),
+                          "bytes_per_step_all_ranks": nbytes, "per_rank": f"{T} x {D} f32 in and out",
+                          "numa_bind": not args.no_numa_bind, "ranks": locs}), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 
@@ -291,6 +401,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         uid = [ltxb.Comm.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         comm = ltxb.Comm(uid[0], rank, world, local_rank)
+    # the host pipe's pinned buffers go on this GPU's NUMA node
+    locality = bind_to_gpu_numa(local_rank) if not args.no_numa_bind else gpu_host_locality(local_rank)
     data, ent = make_blob(dev)
     w = ltxb.build_quant_bufs(ltxb.Blob.from_bytes(data, ent), 0, qset=ltxb.QSET_EXT, hidden=D, ff=FF,
                               device=local_rank)
@@ -443,7 +555,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                     "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": T_TOTAL * D * 4,
                     "d2h_bytes_per_step": T_TOTAL * D * 4, "steps": e2e_steps,
                     "api": "ltxb_block_forward_host (pinned host x in, block output out, copies pipelined)",
-                    "output_matches_device_run": e2e_ok},
+                    "output_matches_device_run": e2e_ok,
+                    "host_placement": {"numa_bind": not args.no_numa_bind, "rank0": locality}},
             "structural": structural,
             "gpu_launches": launches,
             "gpu_launches_per_step": launches // max(1, args.steps),
@@ -452,6 +565,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         }
         if world == 1 and not args.no_cpu:
             try:
+                os.sched_setaffinity(0, range(os.cpu_count() or 1))  # the CPU baseline gets every core
                 # ~10-20 s of timed CPU work: passes over the four sample token counts
                 r = cpu_block_sample(100, 1, budget_s=12.0)
                 line["cpu_baseline"] = {"value": round(r["tflops"], 4), "unit": "TFLOP/s", "cores": r["cores"],
@@ -584,6 +698,10 @@ def main() -> int:
     ap.add_argument("--blocks", type=int, default=48, help="--denoise: blocks per step")
     ap.add_argument("--denoise-steps", type=int, default=8, help="--denoise: distilled steps (<= 8)")
     ap.add_argument("--distinct", type=int, default=4, help="--denoise: distinct uploaded weight sets")
+    ap.add_argument("--copy-only", action="store_true",
+                    help="instead of the block metric, time the host copies of the end-to-end pipe alone")
+    ap.add_argument("--no-numa-bind", action="store_true",
+                    help="leave each rank's pinned host buffers wherever the OS places them")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -596,6 +714,8 @@ def main() -> int:
         return run_reference(args, rank, world)
     if args.denoise:
         return run_denoise(args, rank, world, local_rank)
+    if args.copy_only:
+        return run_copy(args, rank, world, local_rank)
     return run_ours(args, rank, world, local_rank)
 
 

@@ -53,6 +53,26 @@ constexpr int AT_SMEM = 1024 + 2 * AT_TILE /*Q_A,Q_B*/ + 2 * AT_STAGES * AT_TILE
                         (2 * 2 * 2 + 2 * 2) * AT_BM * 4 /*row-max (x2 buffers) and row-sum exchange*/;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when the max grows by > 2^8
 
+// How many of the 16 exponential pairs of a 32-column chunk run as the
+// polynomial on the FMA pipe (the rest on MUFU), spread evenly over the
+// chunk. A build-time parameter: the best split depends on whether the
+// kernel runs at full clock or at the board's power limit.
+#ifndef LTXB_EXP_POLY_PAIRS
+#define LTXB_EXP_POLY_PAIRS 2
+#endif
+// bit e set: pair e of the chunk on the polynomial (1, 2, 3, 4, 6, 8 or 16 pairs)
+__host__ __device__ constexpr uint32_t poly_pair_mask(int n) {
+  return n <= 0 ? 0u
+       : n == 1 ? 0x0020u
+       : n == 2 ? 0x2020u
+       : n == 3 ? 0x2084u
+       : n == 4 ? 0x2222u
+       : n == 6 ? 0x2A2Au
+       : n == 8 ? 0xAAAAu
+                : 0xFFFFu;
+}
+constexpr uint32_t kPolyMask = poly_pair_mask(LTXB_EXP_POLY_PAIRS);
+
 __device__ __forceinline__ float ex2_mufu(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -395,7 +415,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           up2(fma2(pk2(__uint_as_float(cv[2 * e]), __uint_as_float(cv[2 * e + 1])), c2, nm2), a0, a1);
           // 1 of every 8 pairs on the FMA pipe (packed polynomial), the rest on
           // MUFU: the best balance measured under the board's power limit
-          if ((e & 7) == 5) {
+          if ((kPolyMask >> e) & 1u) {
             ex2_poly2(a0, a1, p0, p1);
           } else {
             p0 = ex2_mufu(a0);

@@ -95,9 +95,14 @@ def write_dir(directory, tensors, block: int = 0, provenance: dict | None = None
     blob.bin and blob_manifest.json (align, block, total_bytes, blob_sha256,
     entries with their own sha256, plus `provenance` fields such as repo and
     revision). Returns the manifest."""
+    blob, entries = pack(tensors)
+    return write_packed(directory, blob, entries, block, provenance)
+
+
+def write_packed(directory, blob: bytes, entries: list, block: int = 0, provenance: dict | None = None) -> dict:
+    """write_dir for a blob already packed (e.g. by synthetic_block)."""
     d = pathlib.Path(directory)
     d.mkdir(parents=True, exist_ok=True)
-    blob, entries = pack(tensors)
     man = dict(packer_version=1, packer_commit="ltxb", align=ALIGN, block=block, repo="", revision="",
                source_file="", model_version="")
     man.update(provenance or {})

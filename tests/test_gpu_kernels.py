@@ -205,3 +205,33 @@ def test_bounded_wait_expires_and_context_survives(cuda):
     assert ref.rel_rms(out.float().cpu(), _attn_ref(q, q, q)) < ATTN_TOL
     with pytest.raises(ltxb.LtxbError):
         ltxb.selftest_wait(0)
+
+
+@pytest.mark.parametrize("K,N", [(4096, 4096), (4096, 12288), (4096, 16384), (16384, 4096)])
+def test_dq_gemm_config2_full_m_sampled_rows(cuda, K, N):
+    """BASELINE config 2 at its full size: M = 28,160 bf16 N(0, 1) rows, W
+    N(0, 0.02) with 0.5% of input channels x20, int8 g128 with bf16 scales,
+    bf16 output -- through the expand-then-GEMM path the block uses. 256
+    sampled rows (both edge tiles included) against f64 on the exactly
+    dequantised weights; every row finite."""
+    import ltxb
+    M = 28160
+    seed = 2000 + K + N
+    w = oin.apply_outliers(oin.normal_f32(seed, "c2w", (N, K), 0.02), seed, "c2w")
+    q, sc = ref.quantize_g128(w, scale_dtype="bf16")
+    g = torch.Generator(device=cuda).manual_seed(seed)
+    a = torch.randn(M, K, generator=g, device=cuda).to(torch.bfloat16)
+    wq = torch.from_numpy(q).to(cuda)
+    s = torch.from_numpy(sc.view(np.int16)).to(cuda).view(torch.bfloat16)
+    out = ltxb.dq_gemm(a, wq, s, None, fused=False)
+    torch.cuda.synchronize()
+    assert ltxb.device_status() == ltxb.OK
+    rng = np.random.default_rng(seed)
+    rows = np.unique(np.concatenate([[0, 127, 128, M - 129, M - 128, M - 1], rng.choice(M, 250, replace=False)]))
+    idx = torch.from_numpy(rows).to(cuda)
+    got = out.index_select(0, idx).double().cpu()
+    want = a.index_select(0, idx).double().cpu() @ torch.from_numpy(ref.dequant(q, sc)).T
+    err = ref.rel_rms(got, want)
+    print(f"\nconfig 2 K={K} N={N} M={M}: rel-RMS {err:.2e} on {len(rows)} rows")
+    assert err < GEMM_TOL
+    assert bool(torch.isfinite(out).all())

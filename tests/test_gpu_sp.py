@@ -188,3 +188,85 @@ def test_sp_denoise_loop_matches_single_gpu_and_oracle():
     assert ref.rel_rms(sp, want) <= tol
     assert ref.rel_rms(single, want) <= tol
     assert ref.rel_rms(sp, single) < 3e-3
+
+
+def _depart_worker(rank, world, uid, gone, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import sys
+    import time
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "ltx-zml_b200"), os.path.join(root, "tests")]
+    import ltxb
+    import helpers as h
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        geom, bw, data, ent, _ = h.weights_case(D, FF, 3, "int8")
+        inp = h.inputs_case(D, (2, 4, 32), S, 3, "axes", 3, "random")
+        w = h.upload(data, ent, geom, ltxb.MODE_INT8, device=rank)
+        full = h.to_cuda(inp, dev)
+        T = full[0].shape[0] // world
+        sl = slice(rank * T, (rank + 1) * T)
+        x, tstab, tidx, ctx, pts2, cos, sin = full
+        part = (x[sl].contiguous(), tstab, tidx[sl].contiguous(), ctx, pts2, cos[sl].contiguous(),
+                sin[sl].contiguous())
+        comm = ltxb.Comm(uid, rank, world, rank)
+        ltxb.Block(w, comm).forward(*part)
+        torch.cuda.synchronize()  # nothing of this rank is in flight from here on
+        if rank == 1:
+            q.put((rank, "left", None))
+            gone.set()
+            os._exit(0)  # leaves between block calls without freeing anything
+        if not gone.wait(timeout=120):  # the survivor learns of it on the host
+            q.put((rank, None, "no departure signal"))
+            return
+        check = "ok"
+        try:
+            comm.check()
+        except ltxb.LtxbError as e:
+            check = f"error {e.code}"
+        t0 = time.time()
+        comm.abort()  # frees the group without waiting for the peer
+        dt = time.time() - t0
+        # the context stays usable: the whole block on this GPU alone
+        out = ltxb.Block(w).forward(*full)
+        torch.cuda.synchronize()
+        q.put((rank, dict(check=check, abort_s=dt, status=ltxb.device_status(),
+                          finite=bool(torch.isfinite(out).all())), None))
+        w.free()
+    except Exception as exc:  # report, never hang the parent
+        q.put((rank, None, repr(exc)))
+
+
+def test_departing_rank_survivor_aborts_and_continues():
+    """A rank leaves between block calls (none of its kernels or collectives
+    in flight) and says so on the host; the other rank's communicator check
+    returns, ltxb_comm_abort returns promptly, and the same context then runs
+    a single-GPU block normally -- the reference's Ring.abort / reader_err
+    propagation (ltx/loader.zig:199-202, :240-247, :308-313) across ranks."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import ltxb
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    gone = ctx.Event()
+    uid = ltxb.Comm.unique_id()
+    procs = [ctx.Process(target=_depart_worker, args=(r, 2, uid, gone, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in procs:
+            r, val, err = q.get(timeout=300)
+            assert err is None, f"rank {r}: {err}"
+            res[r] = val
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+    assert res[1] == "left"
+    s = res[0]
+    print(f"\nsurvivor: check {s['check']}, abort {s['abort_s']:.3f} s, status {s['status']}")
+    assert s["abort_s"] < 30.0
+    assert s["status"] == 0 and s["finite"]
