@@ -70,6 +70,7 @@ struct Ws {
 struct Bufs {
   // activations: bf16 in tensor-core modes, f32 in f32 mode (`act` elem size)
   void* n = nullptr;      // [T, D]   norm-modulate output (reused: attn_in, ff_in)
+  float* mod = nullptr;   // [3][K][2][D] combined modulation rows of the three norms (small K)
   void* qkv = nullptr;    // [T, 3D]
   float* ssq = nullptr;   // [T, 32]  q/k row sums of squares per N tile
   void* q = nullptr;      // [T, D]
@@ -101,6 +102,8 @@ struct Bufs {
 };
 
 static bool g_fused_dequant = false;  // int8 GEMMs: dequantise in smem (true) or expand first (false)
+// modulation tables with at most this many rows get combined once per call
+constexpr int kModTableRows = 64;
 
 // Sequence-parallel self-attention, three exchanges:
 //   SP_ALLTOALL  head-parallel: q/k/v go to the rank that owns their heads
@@ -148,6 +151,7 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
   const size_t Tt = (size_t)c->T * (c->sp_size > 1 ? c->sp_size : 1);
   const size_t act = (w->mode == LTXB_MODE_F32) ? 4 : 2;
   b.n = ws.take<uint8_t>(T * D, act);
+  if (c->K <= kModTableRows) b.mod = ws.take<float>((size_t)3 * c->K * 2 * D);
   b.qkv = ws.take<uint8_t>(T * 3 * D, act);
   b.ssq = ws.take<float>(T * 32);
   const bool sp = c->sp_size > 1;
@@ -559,9 +563,20 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   // 1. n = modulate(rms(x), ada1, ada0)
   if (stage == LTXB_STAGE_S1_NORM_MSA)
     return norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, c->K, 0, 1, stage_out, 1, nullptr, st);
+  // the three norms' modulation rows, combined once: (0, 1) attention input,
+  // (6, 7) cross-attention query input, (3, 4) FFN input
+  const size_t mod_stride = (size_t)c->K * 2 * D;
+  if (b.mod) {
+    const int shifts[3] = {0, 6, 3}, scales[3] = {1, 7, 4};
+    CK(mod_tables(w->sst, io->tstab, c->K, D, shifts, scales, 3, b.mod, st));
+  }
+  auto norm = [&](const float* xin, int which, int r_shift, int r_scale) {
+    if (b.mod) return norm_modulate_tab(xin, T, D, b.mod + which * mod_stride, io->tidx, c->K, b.n, f32, st);
+    return norm_modulate(xin, T, D, w->sst, io->tstab, io->tidx, c->K, r_shift, r_scale, b.n, f32, nullptr, st);
+  };
   {
     Phase p("norm_msa", st);
-    CK(norm_modulate(io->x, T, D, w->sst, io->tstab, io->tidx, c->K, 0, 1, b.n, f32, nullptr, st));
+    CK(norm(io->x, 0, 0, 1));
   }
   // 2. fused q/k/v projection (+ q/k sums of squares)
   {
@@ -683,7 +698,7 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
   // 7. cross-attention query input
   {
     Phase p("norm_ca", st);
-    CK(norm_modulate(b.x_sa, T, D, w->sst, io->tstab, io->tidx, c->K, 6, 7, b.n, f32, nullptr, st));
+    CK(norm(b.x_sa, 1, 6, 7));
   }
   // 8. prompt K/V (computed before self-attention under sequence
   // parallelism, where it overlaps the q/k/v exchange; it reads neither x
@@ -726,7 +741,7 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
     return norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, c->K, 3, 4, stage_out, 1, nullptr, st);
   {
     Phase p("norm_mlp", st);
-    CK(norm_modulate(b.x_ca, T, D, w->sst, io->tstab, io->tidx, c->K, 3, 4, b.n, f32, nullptr, st));
+    CK(norm(b.x_ca, 2, 3, 4));
   }
   // 14. h = gelu(f W1^T)
   {

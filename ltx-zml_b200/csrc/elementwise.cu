@@ -143,6 +143,113 @@ __global__ void __launch_bounds__(ROW_THREADS, 8) norm_modulate_reg_kernel(
   }
 }
 
+// The modulation rows of up to three norm-modulate calls, combined once per
+// block call: tab[n][k][0] = (sst[scale_n] + tstab[k, scale_n]) + 1 and
+// tab[n][k][1] = sst[shift_n] + tstab[k, shift_n], the same f32 operations
+// norm_modulate does per element, so results are bit-identical.
+struct ModRows {
+  int shift[3], scale[3];
+};
+__global__ void mod_tables_kernel(const float* __restrict__ sst, const float* __restrict__ tstab, int tk, int D,
+                                  ModRows rows, int n, float* __restrict__ tab) {
+  const size_t total = (size_t)n * tk * D;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % D);
+    const int k = (int)((i / D) % tk);
+    const int m = (int)(i / ((size_t)tk * D));
+    const int rs = rows.scale[m], rh = rows.shift[m];
+    float* o = tab + (((size_t)m * tk + k) * 2) * D + c;
+    o[0] = (tstab[((size_t)k * 9 + rs) * D + c] + sst[(size_t)rs * D + c]) + 1.0f;
+    o[D] = tstab[((size_t)k * 9 + rh) * D + c] + sst[(size_t)rh * D + c];
+  }
+}
+
+int mod_tables(const float* sst, const float* tstab, int tk, int D, const int* shifts, const int* scales, int n,
+               float* tab, cudaStream_t st) {
+  if (n < 1 || n > 3 || tk < 1) return set_error(LTXB_EINVAL, "mod_tables: 1..3 tables, tk >= 1");
+  ModRows r{};
+  for (int i = 0; i < n; ++i) {
+    r.shift[i] = shifts[i];
+    r.scale[i] = scales[i];
+  }
+  const size_t total = (size_t)n * tk * D;
+  int grid = (int)((total + 255) / 256);
+  if (grid > 4 * sm_count()) grid = 4 * sm_count();
+  mod_tables_kernel<<<grid, 256, 0, st>>>(sst, tstab, tk, D, r, n, tab);
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_error(LTXB_ECUDA, "mod_tables: %s", cudaGetErrorString(e));
+}
+
+// norm_modulate_reg_kernel with the modulation rows read from a combined
+// table (two loads per four columns instead of four).
+template <int V>
+__global__ void __launch_bounds__(ROW_THREADS, 8) norm_modulate_tab_kernel(
+    const float* __restrict__ x, int D, const float* __restrict__ tab, const int* __restrict__ tidx, int tk,
+    void* __restrict__ out, int out_f32) {
+  __shared__ float red[ROW_THREADS / 32];
+  const int t = blockIdx.x;
+  const int nv = D >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * D);
+  float4 v[V];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = threadIdx.x + j * ROW_THREADS;
+    v[j] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    ss = fmaf(v[j].x, v[j].x, ss);
+    ss = fmaf(v[j].y, v[j].y, ss);
+    ss = fmaf(v[j].z, v[j].z, ss);
+    ss = fmaf(v[j].w, v[j].w, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < ROW_THREADS / 32; ++i) ss += red[i];
+  const float r = rsqrtf(ss / (float)D + kEps);
+  const int trow = table_row(tidx, t, tk);
+  const float4* sc4 = reinterpret_cast<const float4*>(tab + (size_t)trow * 2 * D);
+  const float4* sh4 = sc4 + nv;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = threadIdx.x + j * ROW_THREADS;
+    if (i >= nv) break;
+    const float4 sc = __ldg(sc4 + i), sh = __ldg(sh4 + i);
+    float4 o;
+    o.x = v[j].x * r * sc.x + sh.x;
+    o.y = v[j].y * r * sc.y + sh.y;
+    o.z = v[j].z * r * sc.z + sh.z;
+    o.w = v[j].w * r * sc.w + sh.w;
+    if (out_f32)
+      reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * D)[i] = o;
+    else
+      reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)t * D)[i] =
+          make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
+  }
+}
+
+int norm_modulate_tab(const float* x, int T, int D, const float* tab, const int* tidx, int tk, void* out, int out_f32,
+                      cudaStream_t st) {
+  if (T <= 0) return LTXB_OK;
+  const int v = (D / 4 + ROW_THREADS - 1) / ROW_THREADS;
+  if (D % 4 || v > 4) return set_error(LTXB_EINVAL, "norm_modulate_tab: D must be a multiple of 4, at most 4096");
+  switch (v) {
+    case 1: norm_modulate_tab_kernel<1><<<T, ROW_THREADS, 0, st>>>(x, D, tab, tidx, tk, out, out_f32); break;
+    case 2: norm_modulate_tab_kernel<2><<<T, ROW_THREADS, 0, st>>>(x, D, tab, tidx, tk, out, out_f32); break;
+    case 3: norm_modulate_tab_kernel<3><<<T, ROW_THREADS, 0, st>>>(x, D, tab, tidx, tk, out, out_f32); break;
+    default: norm_modulate_tab_kernel<4><<<T, ROW_THREADS, 0, st>>>(x, D, tab, tidx, tk, out, out_f32); break;
+  }
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "norm_modulate_tab");
+}
+
 int norm_modulate(const float* x, int T, int D, const float* sst, const float* tstab, const int* tidx, int tk, int r_shift,
                   int r_scale, void* out, int out_f32, float* rms_copy, cudaStream_t st) {
   if (T <= 0) return LTXB_OK;
@@ -370,32 +477,50 @@ int ctx_modulate(const float* ctx, int S, int D, const float* psst, const float*
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "ctx_modulate");
 }
 
-// int8 [N, K] x scale[N, K/128] -> bf16 [N, K]; 16 weights per thread step.
-__global__ void dequant_weights_kernel(const int8_t* __restrict__ q, const void* __restrict__ scales, int scale_bf16,
-                                       int N, int K, __nv_bfloat16* __restrict__ out) {
-  const size_t n16 = (size_t)N * K / 16;
-  const int G = K / 128;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
-    const size_t e0 = i * 16;
-    const size_t row = e0 / K;
-    const int g = (int)((e0 % K) >> 7);
-    const float s = scale_bf16
-                        ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(scales)[row * G + g] << 16)
-                        : reinterpret_cast<const float*>(scales)[row * G + g];
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(q) + i);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[8];
+// int8 [N, K] x scale[N, K/128] -> bf16 [N, K]; 16 weights per chunk, four
+// chunks per thread in flight (their loads issued before any arithmetic).
+__device__ __forceinline__ float dq_scale(const void* scales, int scale_bf16, size_t si) {
+  return scale_bf16 ? __uint_as_float((uint32_t)__ldg(reinterpret_cast<const uint16_t*>(scales) + si) << 16)
+                    : __ldg(reinterpret_cast<const float*>(scales) + si);
+}
+
+__device__ __forceinline__ void dq_store16(uint4 v, float s, __nv_bfloat16* out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int8_t b0 = (int8_t)(w[j] & 0xFF), b1 = (int8_t)((w[j] >> 8) & 0xFF);
-      const int8_t b2 = (int8_t)((w[j] >> 16) & 0xFF), b3 = (int8_t)(w[j] >> 24);
-      o[2 * j] = pack_bf16x2((float)b0 * s, (float)b1 * s);
-      o[2 * j + 1] = pack_bf16x2((float)b2 * s, (float)b3 * s);
-    }
-    uint4* op = reinterpret_cast<uint4*>(out + e0);
-    op[0] = make_uint4(o[0], o[1], o[2], o[3]);
-    op[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  for (int j = 0; j < 4; ++j) {
+    const int8_t b0 = (int8_t)(w[j] & 0xFF), b1 = (int8_t)((w[j] >> 8) & 0xFF);
+    const int8_t b2 = (int8_t)((w[j] >> 16) & 0xFF), b3 = (int8_t)(w[j] >> 24);
+    o[2 * j] = pack_bf16x2((float)b0 * s, (float)b1 * s);
+    o[2 * j + 1] = pack_bf16x2((float)b2 * s, (float)b3 * s);
   }
+  uint4* op = reinterpret_cast<uint4*>(out);
+  op[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  op[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__global__ void __launch_bounds__(256, 4) dequant_weights_kernel(const int8_t* __restrict__ q,
+                                                              const void* __restrict__ scales, int scale_bf16, int N,
+                                                              int K, __nv_bfloat16* __restrict__ out) {
+  const size_t n16 = (size_t)N * K / 16;
+  const int G = K / 128, c16 = K / 16;  // chunks per row
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    uint4 v[4];
+    float sc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const size_t c = i + u * stride;
+      v[u] = __ldg(reinterpret_cast<const uint4*>(q) + c);
+      sc[u] = dq_scale(scales, scale_bf16, (c / c16) * G + ((c % c16) >> 3));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) dq_store16(v[u], sc[u], out + (i + u * stride) * 16);
+  }
+  for (; i < n16; i += stride)
+    dq_store16(__ldg(reinterpret_cast<const uint4*>(q) + i), dq_scale(scales, scale_bf16, (i / c16) * G + ((i % c16) >> 3)),
+               out + i * 16);
 }
 
 int dequant_weights(const int8_t* q, const void* scales, int scale_bf16, int N, int K, void* out, cudaStream_t st) {

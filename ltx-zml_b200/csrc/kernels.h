@@ -127,6 +127,13 @@ cudaError_t attn_status(uint32_t* v, bool clear);
 // n = rms(x) * (1 + ada(r_scale)) + ada(r_shift) -> bf16 or f32 [T, D]; tstab has tk rows
 int norm_modulate(const float* x, int T, int D, const float* sst, const float* tstab, const int* tidx, int tk, int r_shift,
                   int r_scale, void* out, int out_f32, float* rms_copy, cudaStream_t st);
+// combined modulation rows of n (<= 3) norm-modulate calls: tab [n][tk][2][D]
+// = ((sst + tstab)[scale] + 1, (sst + tstab)[shift]) per table row
+int mod_tables(const float* sst, const float* tstab, int tk, int D, const int* shifts, const int* scales, int n,
+               float* tab, cudaStream_t st);
+// norm_modulate from one table of mod_tables (tab points at its [tk][2][D])
+int norm_modulate_tab(const float* x, int T, int D, const float* tab, const int* tidx, int tk, void* out, int out_f32,
+                      cudaStream_t st);
 // weightless rms only (s4_normed stage), f32 out
 int rms_rows(const float* x, int T, int D, float* out, cudaStream_t st);
 // q/k norm (+ optional RoPE) from raw bf16 projections and per-tile sums of squares
