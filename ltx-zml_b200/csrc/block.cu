@@ -366,98 +366,113 @@ static int ring_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, 
 // compute stream runs that group's split-K/V attention as soon as its gather
 // has landed: the gathers of later groups overlap the attention of earlier
 // ones.
-// Head-parallel (all-to-all) variant. Rank r owns heads [r H/N, (r+1) H/N).
+// Head-parallel (all-to-all) variant. Rank r owns heads [r H/N, (r+1) H/N),
+// processed in SG sub-groups of 4 heads (a sub-group's attention over all
+// tokens is 4 x 110 query-tile pairs at T 28,160: whole waves on 148 SMs).
 // 1. q, k (this rank's tokens, already normalised and rotated) and v are
-//    regrouped into [x][N][T][D/N] so that the block for rank p is
-//    contiguous; one NCCL group sends block p to rank p and receives rank
-//    p's block for this rank's heads (rank p's tokens are tokens
-//    [p T, (p+1) T), so the received blocks stack into [N T][D/N] in token
-//    order); the gate logits [T, G] are all-gathered in the same group.
-// 2. Attention over all N T queries and keys for this rank's H/N heads
-//    (the single-GPU kernel: no split states, whole waves).
-// 3. A second group returns rows [p T, (p+1) T) of the output to rank p,
-//    and the received [N][T][D/N] blocks are placed into the [T, D]
-//    attention output.
-// The caller's stream waits on the comm stream after each exchange, so the
-// comm stream is idle whenever the caller's stream is.
+//    regrouped into [SG][x][N][T][Dg] (Dg = 4 x 128), so that every
+//    (sub-group, tensor, rank) block is contiguous. Per sub-group, one NCCL
+//    group sends block p to rank p and receives rank p's block for this
+//    rank's heads; rank p's tokens are tokens [p T, (p+1) T), so the
+//    received blocks stack into [N T][Dg] in token order. The gate logits
+//    [T, G] are all-gathered first.
+// 2. Per sub-group, attention over all N T queries and keys for its heads
+//    (the single-GPU kernel), as soon as that sub-group has arrived: it
+//    overlaps the transfer of the later sub-groups.
+// 3. Per sub-group, a group returns rows [p T, (p+1) T) of its output to
+//    rank p while the next sub-group computes; the received
+//    [SG][N][T][Dg] blocks are placed into the [T, D] attention output.
+// The caller's stream waits on the comm stream after the last exchange, so
+// the comm stream is idle whenever the caller's stream is.
 // a2a_start enqueues step 1 (the caller's stream only records an event the
-// comm stream waits on); a2a_finish waits for it and runs steps 2-3. Work
-// that needs neither can run on the caller's stream in between.
+// comm stream waits on); a2a_finish runs steps 2-3. Work that needs neither
+// can run on the caller's stream in between.
+static int a2a_subgroups(const ltxb_weights* w, const ltxb_config* c) {
+  const int hn = w->H / c->sp_size;
+  return hn % 4 == 0 ? hn / 4 : 1;
+}
+
 static int a2a_start(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* k,
                      const void* v_local, int ldv_local, const float* gate, cudaStream_t st) {
   ltxb_comm* cm = c->comm;
-  const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D, Dn = D / N;
-  if ((int)cm->ev.size() < 4) return set_error(LTXB_EINVAL, "sp: communicator event pool too small");
-  const size_t blk = (size_t)T * Dn * 2;  // bytes of one [T][D/N] block
+  const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D, SG = a2a_subgroups(w, c);
+  const int Dg = D / N / SG;
+  if ((int)cm->ev.size() < 1 + 3 * SG) return set_error(LTXB_EINVAL, "sp: communicator event pool too small");
+  const size_t blk = (size_t)T * Dg * 2;  // bytes of one [T][Dg] block
   uint8_t* send = static_cast<uint8_t*>(b.a2a_send);
   uint8_t* recv = static_cast<uint8_t*>(b.a2a_recv);
   const void* srcs[3] = {q, k, v_local};
   const int lds[3] = {D, D, ldv_local};
-  if (int rc = sp_regroup(srcs, lds, 3, T, D, N, send, st)) return rc;
+  if (int rc = sp_regroup(srcs, lds, 3, T, D, N, SG, send, st)) return rc;
   cudaEventRecord(cm->ev[0], st);
   cudaStreamWaitEvent(cm->comm_stream, cm->ev[0], 0);
   if (gate) {
     ncclResult_t gr = ncclAllGather(gate, b.gate_all, (size_t)T * w->G, ncclFloat, cm->nccl, cm->comm_stream);
     if (gr != ncclSuccess) return set_error(LTXB_ENCCL, "gate all-gather: %s", ncclGetErrorString(gr));
   }
-  ncclGroupStart();
-  for (int x = 0; x < 3; ++x)
-    for (int p = 0; p < N; ++p) {
-      uint8_t* dst = recv + ((size_t)x * N + p) * blk;
-      const uint8_t* src = send + ((size_t)x * N + p) * blk;
-      if (p == r) continue;
-      ncclSend(src, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
-      ncclRecv(dst, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+  for (int g = 0; g < SG; ++g) {
+    ncclGroupStart();
+    for (int x = 0; x < 3; ++x)
+      for (int p = 0; p < N; ++p) {
+        if (p == r) continue;
+        const size_t off = (((size_t)g * 3 + x) * N + p) * blk;
+        ncclSend(send + off, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+        ncclRecv(recv + off, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+      }
+    ncclResult_t nr = ncclGroupEnd();
+    if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "q/k/v all-to-all: %s", ncclGetErrorString(nr));
+    for (int x = 0; x < 3; ++x) {  // this rank's own block
+      const size_t off = (((size_t)g * 3 + x) * N + r) * blk;
+      cudaError_t e = cudaMemcpyAsync(recv + off, send + off, blk, cudaMemcpyDeviceToDevice, cm->comm_stream);
+      if (e != cudaSuccess) return set_cuda_error(e, "sp: local block");
     }
-  ncclResult_t nr = ncclGroupEnd();
-  if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "q/k/v all-to-all: %s", ncclGetErrorString(nr));
-  for (int x = 0; x < 3; ++x) {  // this rank's own block
-    cudaError_t e = cudaMemcpyAsync(recv + ((size_t)x * N + r) * blk, send + ((size_t)x * N + r) * blk, blk,
-                                    cudaMemcpyDeviceToDevice, cm->comm_stream);
-    if (e != cudaSuccess) return set_cuda_error(e, "sp: local block");
+    cudaEventRecord(cm->ev[1 + g], cm->comm_stream);
   }
-  cudaEventRecord(cm->ev[1], cm->comm_stream);
   return LTXB_OK;
 }
 
 static int a2a_finish(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const float* gate, cudaStream_t st) {
   ltxb_comm* cm = c->comm;
-  const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D, Dn = D / N, Hn = w->H / N;
-  const size_t blk = (size_t)T * Dn * 2;
+  const int N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D, Hn = w->H / N, SG = a2a_subgroups(w, c);
+  const int Dg = D / N / SG, hg = Hn / SG;
+  const size_t blk = (size_t)T * Dg * 2;
   uint8_t* recv = static_cast<uint8_t*>(b.a2a_recv);
-  cudaStreamWaitEvent(st, cm->ev[1], 0);
-  AttnArgs a{};
-  a.q = recv;
-  a.k = recv + (size_t)N * blk;
-  a.v = recv + 2 * (size_t)N * blk;
-  a.ldq = a.ldk = a.ldv = Dn;
-  a.out = b.a2a_o;
-  a.ldo = Dn;
-  a.gate = gate ? b.gate_all + (size_t)r * Hn : nullptr;
-  a.ldg = w->G;
-  a.Tq = N * T;
-  a.Tkv = N * T;
-  a.H = Hn;
-  a.scale = 0.08838834764831845f;
-  if (int rc = attention_tc(a, st)) return rc;
-  cudaEventRecord(cm->ev[2], st);
-  cudaStreamWaitEvent(cm->comm_stream, cm->ev[2], 0);
   uint8_t* o = static_cast<uint8_t*>(b.a2a_o);
   uint8_t* orecv = static_cast<uint8_t*>(b.a2a_orecv);
-  ncclGroupStart();
-  for (int p = 0; p < N; ++p) {
-    if (p == r) continue;
-    ncclSend(o + (size_t)p * blk, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
-    ncclRecv(orecv + (size_t)p * blk, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+  for (int g = 0; g < SG; ++g) {
+    cudaStreamWaitEvent(st, cm->ev[1 + g], 0);
+    AttnArgs a{};
+    a.q = recv + ((size_t)g * 3 + 0) * N * blk;
+    a.k = recv + ((size_t)g * 3 + 1) * N * blk;
+    a.v = recv + ((size_t)g * 3 + 2) * N * blk;
+    a.ldq = a.ldk = a.ldv = Dg;
+    a.out = o + (size_t)g * N * blk;
+    a.ldo = Dg;
+    a.gate = gate ? b.gate_all + (size_t)r * Hn + (size_t)g * hg : nullptr;
+    a.ldg = w->G;
+    a.Tq = N * T;
+    a.Tkv = N * T;
+    a.H = hg;
+    a.scale = 0.08838834764831845f;
+    if (int rc = attention_tc(a, st)) return rc;
+    cudaEventRecord(cm->ev[1 + SG + g], st);
+    cudaStreamWaitEvent(cm->comm_stream, cm->ev[1 + SG + g], 0);
+    ncclGroupStart();
+    for (int p = 0; p < N; ++p) {
+      if (p == r) continue;
+      const size_t off = ((size_t)g * N + p) * blk;
+      ncclSend(o + off, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+      ncclRecv(orecv + off, blk, ncclUint8, p, cm->nccl, cm->comm_stream);
+    }
+    ncclResult_t nr = ncclGroupEnd();
+    if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "attention output all-to-all: %s", ncclGetErrorString(nr));
+    const size_t off = ((size_t)g * N + r) * blk;
+    cudaError_t e = cudaMemcpyAsync(orecv + off, o + off, blk, cudaMemcpyDeviceToDevice, cm->comm_stream);
+    if (e != cudaSuccess) return set_cuda_error(e, "sp: local output block");
   }
-  ncclResult_t nr = ncclGroupEnd();
-  if (nr != ncclSuccess) return set_error(LTXB_ENCCL, "attention output all-to-all: %s", ncclGetErrorString(nr));
-  cudaError_t e = cudaMemcpyAsync(orecv + (size_t)r * blk, o + (size_t)r * blk, blk, cudaMemcpyDeviceToDevice,
-                                  cm->comm_stream);
-  if (e != cudaSuccess) return set_cuda_error(e, "sp: local output block");
-  cudaEventRecord(cm->ev[3], cm->comm_stream);
-  cudaStreamWaitEvent(st, cm->ev[3], 0);
-  return sp_ungroup(orecv, T, D, N, b.o, D, st);
+  cudaEventRecord(cm->ev[1 + 2 * SG], cm->comm_stream);
+  cudaStreamWaitEvent(st, cm->ev[1 + 2 * SG], 0);
+  return sp_ungroup(orecv, T, D, N, SG, b.o, D, st);
 }
 
 static int sp_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* v_local,
@@ -1010,7 +1025,7 @@ int ltxb_comm_init(const void* id, int rank, int nranks, int device, ltxb_comm**
     delete c;
     return set_error(LTXB_ECUDA, "comm stream");
   }
-  c->ev.resize(2 * nranks + 2);
+  c->ev.resize(std::max(2 * nranks + 2, 32));
   for (auto& e : c->ev) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
   *out = c;
   return LTXB_OK;

@@ -584,45 +584,49 @@ int dequant_split(const int8_t* q, const void* scales, int scale_bf16, int N, in
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "dequant_split");
 }
 
-// Head-group regrouping for the sequence-parallel exchange: up to three
-// token-major bf16 matrices [T, D] (row strides ld[x]) -> [x][N][T][D / N]
-// (group p = columns [p D/N, (p + 1) D/N)), and back from [N][T][D / N] to
-// [T, D] (row stride ld_out). 16-byte moves.
+// Head-group regrouping for the sequence-parallel exchange. The columns of
+// a [T, D] matrix split into N rank groups of D/N, each into SG sub-groups of
+// Dg = D / (N SG). sp_regroup: up to three token-major bf16 matrices (row
+// strides ld[x]) -> [SG][x][N][T][Dg], so that every (sub-group, tensor,
+// rank) block is contiguous; sp_ungroup: [SG][N][T][Dg] -> [T, D] (row stride
+// ld_out). 16-byte moves.
 struct RegroupSrc {
   const __nv_bfloat16* p[3];
   int ld[3];
 };
 
-__global__ void sp_regroup_kernel(RegroupSrc src, int nsrc, int T, int D, int N, __nv_bfloat16* __restrict__ dst) {
-  const int Dn = D / N, c8 = Dn / 8;
-  const size_t per = (size_t)N * T * c8;
-  const size_t n = (size_t)nsrc * per;
+__global__ void sp_regroup_kernel(RegroupSrc src, int nsrc, int T, int D, int N, int SG,
+                                  __nv_bfloat16* __restrict__ dst) {
+  const int Dn = D / N, Dg = Dn / SG, c8 = Dg / 8;
+  const size_t blk8 = (size_t)T * c8;  // 16-byte units per block
+  const size_t n = (size_t)SG * nsrc * N * blk8;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-    const int x = (int)(i / per);
-    const size_t j = i % per;
-    const int p = (int)(j / ((size_t)T * c8));
-    const size_t k = j % ((size_t)T * c8);
+    const size_t b = i / blk8, k = i % blk8;  // block index = (g nsrc + x) N + p
+    const int p = (int)(b % N), x = (int)((b / N) % nsrc), g = (int)(b / ((size_t)N * nsrc));
     const int t = (int)(k / c8), c = (int)(k % c8) * 8;
-    const uint4 v = *reinterpret_cast<const uint4*>(src.p[x] + (size_t)t * src.ld[x] + p * Dn + c);
-    *reinterpret_cast<uint4*>(dst + (((size_t)x * N + p) * T + t) * Dn + c) = v;
+    const uint4 v = *reinterpret_cast<const uint4*>(src.p[x] + (size_t)t * src.ld[x] + p * Dn + g * Dg + c);
+    *reinterpret_cast<uint4*>(dst + (b * T + t) * Dg + c) = v;
   }
 }
 
-__global__ void sp_ungroup_kernel(const __nv_bfloat16* __restrict__ src, int T, int D, int N,
+__global__ void sp_ungroup_kernel(const __nv_bfloat16* __restrict__ src, int T, int D, int N, int SG,
                                   __nv_bfloat16* __restrict__ out, int ld_out) {
-  const int Dn = D / N, c8 = Dn / 8;
-  const size_t n = (size_t)N * T * c8;
+  const int Dn = D / N, Dg = Dn / SG, c8 = Dg / 8;
+  const size_t blk8 = (size_t)T * c8;
+  const size_t n = (size_t)SG * N * blk8;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-    const int p = (int)(i / ((size_t)T * c8));
-    const size_t k = i % ((size_t)T * c8);
+    const size_t b = i / blk8, k = i % blk8;  // block index = g N + p
+    const int p = (int)(b % N), g = (int)(b / N);
     const int t = (int)(k / c8), c = (int)(k % c8) * 8;
-    *reinterpret_cast<uint4*>(out + (size_t)t * ld_out + p * Dn + c) =
-        *reinterpret_cast<const uint4*>(src + ((size_t)p * T + t) * Dn + c);
+    *reinterpret_cast<uint4*>(out + (size_t)t * ld_out + p * Dn + g * Dg + c) =
+        *reinterpret_cast<const uint4*>(src + (b * T + t) * Dg + c);
   }
 }
 
-int sp_regroup(const void* const* srcs, const int* lds, int nsrc, int T, int D, int N, void* dst, cudaStream_t st) {
-  if (nsrc < 1 || nsrc > 3 || N < 1 || D % (8 * N)) return set_error(LTXB_EINVAL, "sp_regroup: D must split into 16-byte groups");
+int sp_regroup(const void* const* srcs, const int* lds, int nsrc, int T, int D, int N, int SG, void* dst,
+               cudaStream_t st) {
+  if (nsrc < 1 || nsrc > 3 || N < 1 || SG < 1 || D % (8 * N * SG))
+    return set_error(LTXB_EINVAL, "sp_regroup: D must split into 16-byte groups");
   RegroupSrc s{};
   for (int x = 0; x < nsrc; ++x) {
     s.p[x] = static_cast<const __nv_bfloat16*>(srcs[x]);
@@ -633,19 +637,20 @@ int sp_regroup(const void* const* srcs, const int* lds, int nsrc, int T, int D, 
   if (n == 0) return LTXB_OK;
   int grid = (int)((n + 255) / 256);
   if (grid > 8 * sm_count()) grid = 8 * sm_count();
-  sp_regroup_kernel<<<grid, 256, 0, st>>>(s, nsrc, T, D, N, static_cast<__nv_bfloat16*>(dst));
+  sp_regroup_kernel<<<grid, 256, 0, st>>>(s, nsrc, T, D, N, SG, static_cast<__nv_bfloat16*>(dst));
   launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "sp_regroup");
 }
 
-int sp_ungroup(const void* src, int T, int D, int N, void* out, int ld_out, cudaStream_t st) {
-  if (N < 1 || D % (8 * N) || ld_out % 8) return set_error(LTXB_EINVAL, "sp_ungroup: D must split into 16-byte groups");
+int sp_ungroup(const void* src, int T, int D, int N, int SG, void* out, int ld_out, cudaStream_t st) {
+  if (N < 1 || SG < 1 || D % (8 * N * SG) || ld_out % 8)
+    return set_error(LTXB_EINVAL, "sp_ungroup: D must split into 16-byte groups");
   const size_t n = (size_t)T * (D / 8);
   if (n == 0) return LTXB_OK;
   int grid = (int)((n + 255) / 256);
   if (grid > 8 * sm_count()) grid = 8 * sm_count();
-  sp_ungroup_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), T, D, N,
+  sp_ungroup_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), T, D, N, SG,
                                           static_cast<__nv_bfloat16*>(out), ld_out);
   launched();
   cudaError_t e = cudaGetLastError();

@@ -175,10 +175,12 @@ int split_f32_bf16(const float* in, int rows, int cols, int parts, void* out, cu
 // w_hi = bf16(q s) and w_lo = bf16(q s - w_hi): q s has at most 15
 // significant bits (bf16 scales), so w_hi + w_lo = q s exactly
 int dequant_split(const int8_t* q, const void* scales, int scale_bf16, int N, int K, void* out, cudaStream_t st);
-// sequence-parallel head-group layout: nsrc (<= 3) bf16 [T, D] matrices with
-// row strides lds -> dst [nsrc][N][T][D/N]; and [N][T][D/N] -> out [T, D]
-int sp_regroup(const void* const* srcs, const int* lds, int nsrc, int T, int D, int N, void* dst, cudaStream_t st);
-int sp_ungroup(const void* src, int T, int D, int N, void* out, int ld_out, cudaStream_t st);
+// sequence-parallel head-group layout (rank groups of D/N columns, each in
+// SG sub-groups of Dg = D/(N SG)): nsrc (<= 3) bf16 [T, D] matrices with row
+// strides lds -> dst [SG][nsrc][N][T][Dg]; and [SG][N][T][Dg] -> out [T, D]
+int sp_regroup(const void* const* srcs, const int* lds, int nsrc, int T, int D, int N, int SG, void* dst,
+               cudaStream_t st);
+int sp_ungroup(const void* src, int T, int D, int N, int SG, void* out, int ld_out, cudaStream_t st);
 // rows x cols f32 (row stride ld_in) -> bf16 (row stride ld_out)
 int cast_rows_f32_bf16(const float* in, int ld_in, void* out, int ld_out, int rows, int cols, cudaStream_t st);
 
