@@ -39,6 +39,8 @@ import torch  # noqa: E402
 
 T_TOTAL, GRID, S, D, FF, H = 28160, (22, 32, 40), 128, 4096, 16384, 32
 METRIC = "dit_block_tflops_28k_int8w"
+# the library's default sequence-parallel exchange (LTXB_SP unset)
+SP_DEFAULT = "alltoall"
 # token counts of the CPU samples (latent grids with T % 1024 == 0, so the
 # restated whileSdpa runs its production chunk of 1024 on every sample)
 CPU_SAMPLE_GRIDS = ((8, 8, 16), (16, 8, 16), (12, 16, 16), (16, 16, 16))
@@ -536,9 +538,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 if top in tj:
                     roofline["traffic"] = tj[top]["bytes_per_launch"]
             roofline["peak_source"] = pk["source"] + " (MEASURED_PEAKS.json; sustained for a kernel inside a long step)"
-        env_sp = "ring" if os.environ.get("LTXB_SP_RING") == "1" else os.environ.get("LTXB_SP", "alltoall")
-        sp_algo = {"ring": "send/recv ring of K/V shards", "allgather": "head-group pipelined K/V all-gather"}.get(
-            env_sp, "head-parallel all-to-all: q/k/v to the ranks owning their heads, outputs back")
+        env_sp = "ring" if os.environ.get("LTXB_SP_RING") == "1" else os.environ.get("LTXB_SP", "")
+        if env_sp not in ("ring", "allgather", "alltoall", "peer"):
+            env_sp = SP_DEFAULT if (SP_DEFAULT != "peer" or (comm is not None and comm.peer_mapped())) else "alltoall"
+        sp_algo = {"ring": "send/recv ring of K/V shards", "allgather": "head-group pipelined K/V all-gather",
+                   "peer": "head-parallel, q/k/v and attention rows stored straight into the other GPUs' memory"}.get(
+            env_sp, "head-parallel all-to-all over NCCL send/recv: q/k/v to the ranks owning their heads, outputs back")
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",

@@ -232,8 +232,17 @@ typedef struct ltxb_comm ltxb_comm;
 int ltxb_comm_id_bytes(void);
 /* Rank 0: fill `id` (ltxb_comm_id_bytes() bytes). */
 int ltxb_comm_get_id(void* id);
-/* Every rank: join the group (NCCL over NVLink; one rank per GPU). */
+/* Every rank: join the group (NCCL over NVLink; one rank per GPU). With
+ * 2..8 ranks in separate processes it also maps a window of device memory of
+ * every other rank (CUDA IPC) for the head-parallel exchange over peer
+ * memory; the windows grow, collectively and synchronously, on the first
+ * block call of a new shape. */
 int ltxb_comm_init(const void* id, int rank, int nranks, int device, ltxb_comm** out);
+/* 1 when every rank mapped every other rank's window, so that
+ * sequence-parallel block calls can exchange q/k/v and attention rows by
+ * stores into peer memory; 0 when only the NCCL exchanges are available. No
+ * counterpart in the reference (single device). */
+int ltxb_comm_peer_mapped(const ltxb_comm* c);
 /* Waits for the communicator's queued transfers, then frees it. */
 void ltxb_comm_free(ltxb_comm* c);
 /* The error NCCL has recorded on the communicator, if any

@@ -499,14 +499,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       if (!MERGE) {
         const float g = (row_ok && args.gate) ? args.gate[(size_t)row * args.ldg + h] : 1.0f;
         const float inv = g / lt;
+        // this row's output: here, or (peer exchange) in the window of the
+        // rank that holds the row's token
+        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.out);
+        size_t orow_off = (size_t)row * ldo;
+        if (args.out_tab && row_ok) {
+          const int p = row / args.peer_rows;
+          orow = reinterpret_cast<__nv_bfloat16*>(args.out_tab[p]);
+          orow_off = (size_t)(row - p * args.peer_rows) * ldo + args.out_col0;
+        }
 #pragma unroll 1
         for (int cc = 0; cc < 2; ++cc) {
           uint32_t u[32];
           tmem_ld32(tO + cc * 32, u);
           tmem_wait_ld();
           if (row_ok) {
-            uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * ldo +
-                                                 h * AT_D + hf * 64 + cc * 32);
+            uint4* op = reinterpret_cast<uint4*>(orow + orow_off + h * AT_D + hf * 64 + cc * 32);
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               op[e] = make_uint4(pack_bf16x2(__uint_as_float(u[8 * e + 0]) * inv, __uint_as_float(u[8 * e + 1]) * inv),
@@ -566,6 +574,9 @@ done:
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  // peer exchange: the last CTA tells every rank that its rows have landed
+  // (also after a timed-out wait, so that no rank waits for this one in vain)
+  if (!MERGE && args.sig_counter) last_cta_signal(args.sig_counter, args.sig_tab, args.sig_n, args.sig_epoch);
 }
 
 // out = sum_z O_z 2^(m_z - m) / sum_z l_z 2^(m_z - m) * gate (bf16), m = max_z m_z:

@@ -24,6 +24,7 @@
 #include <nccl.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <string>
@@ -42,11 +43,39 @@ struct ltxb_weights {
   uint64_t bytes = 0;
 };
 
+// Peer window: device memory of this rank that every other rank of the
+// communicator has mapped (CUDA IPC), for the head-parallel exchange over
+// peer memory (peer.cu). Offsets are identical on every rank:
+//   [0, kWinHdr)  header: arrival flags [2 kinds][kMaxPeers] u32 at 0 (kind
+//                 0: q/k/v and gates, 1: attention output; entry p written
+//                 by rank p), CTA counters [2] at 256, and from kWinTab the
+//                 device pointer tables the kernels index, as this process
+//                 maps them: [table][2 parities][kMaxPeers] (orx: every
+//                 rank's output buffer; flago: this rank's kind-1 flag in
+//                 every window)
+//   rx[2]         [3][N][T][D/N] bf16: q, k, v of the owned heads, all tokens
+//   orx[2]        [T][D] bf16: this rank's attention output, all heads
+//   gall[2]       [N T][G] f32: every rank's gate logits
+struct PeerWin {
+  uint8_t* local = nullptr;
+  size_t bytes = 0;
+  std::vector<uint8_t*> base;  // every rank's window as mapped in this process
+  std::vector<char> opened;    // base[p] came from cudaIpcOpenMemHandle
+  size_t off_rx[2] = {}, off_orx[2] = {}, off_gall[2] = {};
+  int T = 0, D = 0, G = 0;     // the shapes the layout was made for
+  uint32_t epoch = 0;          // block calls through the window since it was made
+};
+constexpr size_t kWinHdr = 4096, kWinTab = 1024;
+enum WinTable { TAB_ORX = 0, TAB_FLAGO = 1 };
+
 struct ltxb_comm {
   ncclComm_t nccl = nullptr;
   int rank = 0, nranks = 1, device = 0;
   cudaStream_t comm_stream = nullptr;
   std::vector<cudaEvent_t> ev;  // pool of events for cross-stream ordering
+  bool peer_ok = false;         // every rank mapped every other rank's window
+  PeerWin win;
+  void* xbuf = nullptr;         // [nranks][128] bytes: handle exchange
 };
 
 namespace ltxb {
@@ -113,7 +142,11 @@ constexpr int kModTableRows = 64;
 //                attends its own tokens (LTXB_SP=allgather)
 //   SP_RING      K/V shards passed around a ring (LTXB_SP=ring or
 //                LTXB_SP_RING=1), kept for comparison
-enum SpAlgo { SP_ALLTOALL = 0, SP_ALLGATHER = 1, SP_RING = 2 };
+//   SP_PEER      head-parallel like SP_ALLTOALL, the exchange written as
+//                stores into the other ranks' memory (peer.cu); needs every
+//                rank to have mapped every other rank's window
+//                (LTXB_SP=peer)
+enum SpAlgo { SP_ALLTOALL = 0, SP_ALLGATHER = 1, SP_RING = 2, SP_PEER = 3 };
 static int sp_env_algo() {
   static const int a = [] {
     const char* r = getenv("LTXB_SP_RING");
@@ -122,6 +155,7 @@ static int sp_env_algo() {
     if (e && !strcmp(e, "ring")) return (int)SP_RING;
     if (e && !strcmp(e, "allgather")) return (int)SP_ALLGATHER;
     if (e && !strcmp(e, "alltoall")) return (int)SP_ALLTOALL;
+    if (e && !strcmp(e, "peer")) return (int)SP_PEER;
     return -1;
   }();
   return a;
@@ -131,6 +165,7 @@ static SpAlgo sp_algo(const ltxb_weights* w, const ltxb_config* c) {
   const bool a2a_ok = w->H % n == 0;
   const int e = sp_env_algo();
   if (e == SP_RING || e == SP_ALLGATHER) return static_cast<SpAlgo>(e);
+  if (e == SP_PEER) return SP_PEER;  // the forward call reports it if the windows are missing
   return a2a_ok ? SP_ALLTOALL : SP_ALLGATHER;
 }
 static bool sp_use_ring(const ltxb_weights* w, const ltxb_config* c) { return sp_algo(w, c) == SP_RING; }
@@ -157,9 +192,10 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
   const bool sp = c->sp_size > 1;
   const SpAlgo alg = sp_algo(w, c);
   const bool a2a = sp && alg == SP_ALLTOALL;
+  const bool headpar = a2a || (sp && alg == SP_PEER);  // K of this rank's tokens only
   b.q = ws.take<uint8_t>(T * D, act);
-  b.k = ws.take<uint8_t>((a2a ? T : Tt) * D, act);
-  if (sp && !a2a) b.v = ws.take<uint8_t>(Tt * D, act);
+  b.k = ws.take<uint8_t>((headpar ? T : Tt) * D, act);
+  if (sp && !headpar) b.v = ws.take<uint8_t>(Tt * D, act);
   b.gate = ws.take<float>(T * w->G);
   b.o = ws.take<uint8_t>(T * D, act);
   b.x_sa = ws.take<float>(T * D);
@@ -180,7 +216,7 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
     b.deq_elems = std::max({FF * D, 3 * D * D, 4 * D * D});
     b.deq = ws.take<uint8_t>(b.deq_elems, 2);
   }
-  if (sp && !a2a) {
+  if (sp && !headpar) {
     // split states of one head group (the ring: one state of all heads)
     const size_t ns = sp_kv_splits(w, c), gh = alg == SP_RING ? w->H : w->H / sp_groups(w);
     b.o_acc = ws.take<float>(ns * T * gh * 128);
@@ -475,6 +511,210 @@ static int a2a_finish(const ltxb_weights* w, const ltxb_config* c, Bufs& b, cons
   return sp_ungroup(orecv, T, D, N, SG, b.o, D, st);
 }
 
+// ---- peer window (SP_PEER) ----
+// Closes the other ranks' windows and frees this one (no waiting on peers).
+static void win_release(ltxb_comm* c) {
+  PeerWin& W = c->win;
+  for (size_t p = 0; p < W.base.size(); ++p)
+    if (W.opened[p]) cudaIpcCloseMemHandle(W.base[p]);
+  if (W.local) cudaFree(W.local);
+  W = PeerWin{};
+}
+
+struct WinXchg {
+  cudaIpcMemHandle_t h;
+  uint64_t pid;
+  uint64_t ok;
+};
+static_assert(sizeof(WinXchg) <= 128, "exchange record");
+
+// Collective: every rank allocates a window of `bytes`, the ranks exchange
+// IPC handles through NCCL and map each other's windows. Any earlier window
+// is released first, after a barrier that ends every rank's use of it.
+// Synchronous (the host waits); fails on every rank if any rank failed. The
+// header (flags, counters) starts zeroed and the epoch restarts.
+static int win_setup(ltxb_comm* c, size_t bytes) {
+  const int N = c->nranks, r = c->rank;
+  cudaStream_t cs = c->comm_stream;
+  uint8_t* xb = static_cast<uint8_t*>(c->xbuf);
+  auto fail = [&](int code, const char* what) { return set_error(code, "peer window: %s", what); };
+  cudaDeviceSynchronize();
+  if (c->win.local) {
+    // barrier: every rank's kernels that could still write this window are done
+    if (ncclAllReduce(xb, xb, 1, ncclUint8, ncclMax, c->nccl, cs) != ncclSuccess ||
+        cudaStreamSynchronize(cs) != cudaSuccess)
+      return fail(LTXB_ENCCL, "barrier before release");
+    win_release(c);
+  }
+  WinXchg mine{};
+  mine.pid = (uint64_t)getpid();
+  uint8_t* local = nullptr;
+  bool ok = cudaMalloc(&local, bytes) == cudaSuccess;
+  if (ok) ok = cudaMemset(local, 0, kWinHdr) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+  if (ok) ok = cudaIpcGetMemHandle(&mine.h, local) == cudaSuccess;
+  cudaGetLastError();
+  mine.ok = ok ? 1 : 0;
+  // every transfer of the exchange runs on the comm stream, in order
+  std::vector<uint8_t> all_raw((size_t)N * 128);
+  if (cudaMemcpyAsync(xb + (size_t)r * 128, &mine, sizeof(mine), cudaMemcpyHostToDevice, cs) != cudaSuccess ||
+      ncclAllGather(xb + (size_t)r * 128, xb, 128, ncclUint8, c->nccl, cs) != ncclSuccess ||
+      cudaMemcpyAsync(all_raw.data(), xb, all_raw.size(), cudaMemcpyDeviceToHost, cs) != cudaSuccess ||
+      cudaStreamSynchronize(cs) != cudaSuccess) {
+    if (local) cudaFree(local);
+    return fail(LTXB_ENCCL, "handle exchange");
+  }
+  std::vector<WinXchg> all(N);
+  for (int p = 0; p < N; ++p) memcpy(&all[p], all_raw.data() + (size_t)p * 128, sizeof(WinXchg));
+  PeerWin& W = c->win;
+  W.local = local;
+  W.bytes = bytes;
+  W.base.assign(N, nullptr);
+  W.opened.assign(N, 0);
+  W.base[r] = local;
+  for (int p = 0; p < N && ok; ++p) {
+    if (p == r) continue;
+    // ranks in one process cannot open each other's handles: the window
+    // exchange needs one process per rank
+    if (!all[p].ok || all[p].pid == mine.pid) {
+      ok = false;
+      break;
+    }
+    void* m = nullptr;
+    if (cudaIpcOpenMemHandle(&m, all[p].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = false;
+      break;
+    }
+    W.base[p] = static_cast<uint8_t*>(m);
+    W.opened[p] = 1;
+  }
+  // every rank learns whether all ranks mapped every window
+  uint8_t okb = ok ? 1 : 0;
+  if (cudaMemcpyAsync(xb, &okb, 1, cudaMemcpyHostToDevice, cs) != cudaSuccess ||
+      ncclAllReduce(xb, xb, 1, ncclUint8, ncclMin, c->nccl, cs) != ncclSuccess ||
+      cudaMemcpyAsync(&okb, xb, 1, cudaMemcpyDeviceToHost, cs) != cudaSuccess ||
+      cudaStreamSynchronize(cs) != cudaSuccess)
+    okb = 0;
+  if (!okb) {
+    win_release(c);
+    return fail(LTXB_EUNSUPPORTED, "a rank could not map the other ranks' memory");
+  }
+  return LTXB_OK;
+}
+
+// Makes the window fit a block call of T tokens per rank (collective and
+// synchronous when the shapes change, otherwise free) and writes the device
+// pointer tables the kernels index.
+static int win_prepare(ltxb_comm* c, int T, int D, int G) {
+  PeerWin& W = c->win;
+  if (W.local && W.T == T && W.D == D && W.G == G) return LTXB_OK;
+  const int N = c->nranks, r = c->rank;
+  auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+  size_t off = kWinHdr, o_rx[2], o_orx[2], o_gall[2];
+  for (int i = 0; i < 2; ++i) { o_rx[i] = off; off += al((size_t)3 * N * T * (D / N) * 2); }
+  for (int i = 0; i < 2; ++i) { o_orx[i] = off; off += al((size_t)T * D * 2); }
+  for (int i = 0; i < 2; ++i) { o_gall[i] = off; off += al((size_t)N * T * G * 4); }
+  if (int rc = win_setup(c, off)) return rc;
+  for (int i = 0; i < 2; ++i) {
+    W.off_rx[i] = o_rx[i];
+    W.off_orx[i] = o_orx[i];
+    W.off_gall[i] = o_gall[i];
+  }
+  W.T = T;
+  W.D = D;
+  W.G = G;
+  uint64_t tab[2][2][kMaxPeers] = {};
+  for (int i = 0; i < 2; ++i)
+    for (int p = 0; p < N; ++p) {
+      tab[TAB_ORX][i][p] = reinterpret_cast<uint64_t>(W.base[p] + o_orx[i]);
+      tab[TAB_FLAGO][i][p] = reinterpret_cast<uint64_t>(W.base[p] + (size_t)(1 * kMaxPeers + r) * 4);
+    }
+  if (cudaMemcpyAsync(W.local + kWinTab, tab, sizeof(tab), cudaMemcpyHostToDevice, c->comm_stream) != cudaSuccess ||
+      cudaStreamSynchronize(c->comm_stream) != cudaSuccess)
+    return set_error(LTXB_ECUDA, "peer window: tables");
+  return LTXB_OK;
+}
+
+// SP_PEER, step 1 (before the prompt K/V): this rank's q, k, v and gate
+// logits into the owners' windows, on the comm stream; returns the epoch of
+// this call.
+static int peer_start(const ltxb_weights* w, const ltxb_config* c, const void* q, const void* k, const void* v,
+                      int ldv, const float* gate, cudaStream_t st, uint32_t* epoch) {
+  ltxb_comm* cm = c->comm;
+  if (!cm->peer_ok)
+    return set_error(LTXB_EUNSUPPORTED, "peer exchange: the ranks could not map each other's memory");
+  if (c->sp_size > kMaxPeers || w->H % c->sp_size)
+    return set_error(LTXB_EUNSUPPORTED, "peer exchange: %d ranks, %d heads", c->sp_size, w->H);
+  if (int rc = win_prepare(cm, c->T, w->D, w->G)) return rc;
+  PeerWin& W = cm->win;
+  const uint32_t e = ++W.epoch;
+  const int par = e & 1, N = c->sp_size, r = c->sp_rank;
+  PeerScatterArgs a{};
+  a.src[0] = static_cast<const __nv_bfloat16*>(q);
+  a.src[1] = static_cast<const __nv_bfloat16*>(k);
+  a.src[2] = static_cast<const __nv_bfloat16*>(v);
+  a.ld[0] = a.ld[1] = w->D;
+  a.ld[2] = ldv;
+  a.gate = gate;
+  a.G = w->G;
+  for (int p = 0; p < N; ++p) {
+    a.rx[p] = reinterpret_cast<__nv_bfloat16*>(W.base[p] + W.off_rx[par]);
+    a.gall[p] = reinterpret_cast<float*>(W.base[p] + W.off_gall[par]);
+    a.flag[p] = reinterpret_cast<uint32_t*>(W.base[p] + (size_t)(0 * kMaxPeers + r) * 4);
+  }
+  a.counter = reinterpret_cast<uint32_t*>(W.local + 256);
+  a.epoch = e;
+  a.N = N;
+  a.r = r;
+  a.T = c->T;
+  a.D = w->D;
+  cudaEventRecord(cm->ev[0], st);
+  cudaStreamWaitEvent(cm->comm_stream, cm->ev[0], 0);
+  if (int rc = peer_scatter(a, cm->comm_stream)) return rc;
+  cudaEventRecord(cm->ev[1], cm->comm_stream);
+  *epoch = e;
+  return LTXB_OK;
+}
+
+// SP_PEER, step 2: wait for every rank's q/k/v, attend all N T tokens of the
+// owned heads with the output rows stored straight into their ranks'
+// windows, wait for every rank's output rows. Returns this rank's [T, D]
+// attention output (in its window).
+static int peer_finish(const ltxb_weights* w, const ltxb_config* c, uint32_t e, bool gated, cudaStream_t st,
+                       void** o_out) {
+  ltxb_comm* cm = c->comm;
+  PeerWin& W = cm->win;
+  const int par = e & 1, N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D, Dn = D / N;
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(W.local);
+  cudaStreamWaitEvent(st, cm->ev[1], 0);  // this rank's own slice is written by its scatter
+  if (int rc = peer_wait(flags, N, r, e, 0x301, st)) return rc;
+  const uint8_t* rx = W.local + W.off_rx[par];
+  const size_t blk = (size_t)N * T * Dn * 2;
+  AttnArgs a{};
+  a.q = rx;
+  a.k = rx + blk;
+  a.v = rx + 2 * blk;
+  a.ldq = a.ldk = a.ldv = Dn;
+  a.gate = gated ? reinterpret_cast<const float*>(W.local + W.off_gall[par]) + (size_t)r * (w->H / N) : nullptr;
+  a.ldg = w->G;
+  a.Tq = N * T;
+  a.Tkv = N * T;
+  a.H = w->H / N;
+  a.scale = 0.08838834764831845f;
+  a.ldo = D;
+  a.out_tab = reinterpret_cast<void* const*>(W.local + kWinTab + (size_t)(TAB_ORX * 2 + par) * kMaxPeers * 8);
+  a.peer_rows = T;
+  a.out_col0 = r * Dn;
+  a.sig_counter = reinterpret_cast<uint32_t*>(W.local + 256 + 4);
+  a.sig_tab = reinterpret_cast<uint32_t* const*>(W.local + kWinTab + (size_t)(TAB_FLAGO * 2 + par) * kMaxPeers * 8);
+  a.sig_n = N;
+  a.sig_epoch = e;
+  if (int rc = attention_tc(a, st)) return rc;
+  if (int rc = peer_wait(flags + kMaxPeers, N, r, e, 0x302, st)) return rc;
+  *o_out = W.local + W.off_orx[par];
+  return LTXB_OK;
+}
+
 static int sp_attention(const ltxb_weights* w, const ltxb_config* c, Bufs& b, const void* q, const void* v_local,
                         int ldv_local, const float* gate, cudaStream_t st) {
   const SpAlgo alg = sp_algo(w, c);
@@ -681,7 +921,19 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
 
   // 5. self-attention
   const float* g1 = gated ? b.gate : nullptr;
-  if (sp && alg == SP_ALLTOALL) {
+  void* o_self = b.o;  // self-attention output [T, D]
+  if (sp && alg == SP_PEER) {
+    // q/k/v go into the owners' memory on the comm stream while the prompt
+    // K/V runs here; the attention stores its rows into their ranks' memory
+    uint32_t e = 0;
+    {
+      Phase p("sp_send", st);
+      CK(peer_start(w, c, b.q, b.k, col(b.qkv, 2 * D), 3 * D, g1, st, &e));
+    }
+    CK(prompt_kv());
+    Phase p("attn_self", st);
+    CK(peer_finish(w, c, e, gated, st, &o_self));
+  } else if (sp && alg == SP_ALLTOALL) {
     // the q/k/v exchange runs on the comm stream while the prompt K/V runs here
     {
       Phase p("sp_send", st);
@@ -699,11 +951,11 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
       CK(attn(w, b.q, D, b.k, D, col(b.qkv, 2 * D), 3 * D, b.o, g1, T, T, st));
   }
   if (stage == LTXB_STAGE_S2_ATTN1_NOGATE || stage == LTXB_STAGE_S3_ATTN1)
-    return run_lin(lc, w->o1, b.o, D, T, EPI_F32, stage_out, D);
+    return run_lin(lc, w->o1, o_self, D, T, EPI_F32, stage_out, D);
   // 6. x_sa = x + (o Wo^T + bo) * ada2
   {
     Phase p("gemm_o1", st);
-    CK(run_lin(lc, w->o1, b.o, D, T, EPI_RESID_F32, b.x_sa, D, nullptr, 0, io->x, io->tstab, io->tidx, 2));
+    CK(run_lin(lc, w->o1, o_self, D, T, EPI_RESID_F32, b.x_sa, D, nullptr, 0, io->x, io->tstab, io->tidx, 2));
   }
   if (stage == LTXB_STAGE_S4_AFTER_SA)
     return cudaMemcpyAsync(stage_out, b.x_sa, (size_t)T * D * 4, cudaMemcpyDeviceToDevice, st) == cudaSuccess
@@ -1027,13 +1279,24 @@ int ltxb_comm_init(const void* id, int rank, int nranks, int device, ltxb_comm**
   }
   c->ev.resize(std::max(2 * nranks + 2, 32));
   for (auto& e : c->ev) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+  // the peer-memory exchange: map a header-sized window of every rank now,
+  // so that every rank knows before the first block call (and before any
+  // workspace query) whether the exchange is available; it grows on first use
+  if (nranks > 1 && nranks <= kMaxPeers && cudaMalloc(&c->xbuf, (size_t)nranks * 128) == cudaSuccess)
+    c->peer_ok = win_setup(c, kWinHdr) == LTXB_OK;  // if not, the NCCL exchanges remain
+  cudaGetLastError();
   *out = c;
   return LTXB_OK;
 }
 
+int ltxb_comm_peer_mapped(const ltxb_comm* c) { return c && c->peer_ok ? 1 : 0; }
+
 void ltxb_comm_free(ltxb_comm* c) {
   if (!c) return;
   if (c->comm_stream) cudaStreamSynchronize(c->comm_stream);
+  cudaDeviceSynchronize();  // this rank's kernels that use the peer windows are done
+  win_release(c);
+  if (c->xbuf) cudaFree(c->xbuf);
   for (auto& e : c->ev) cudaEventDestroy(e);
   if (c->nccl) ncclCommDestroy(c->nccl);
   if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
@@ -1055,6 +1318,8 @@ void ltxb_comm_abort(ltxb_comm* c) {
   // abort first: it ends the NCCL kernels still waiting for peers, so the
   // streams and events below no longer depend on a rank that is gone
   if (c->nccl) ncclCommAbort(c->nccl);
+  win_release(c);  // waits only for this rank's kernels, whose peer waits are bounded
+  if (c->xbuf) cudaFree(c->xbuf);
   for (auto& e : c->ev) cudaEventDestroy(e);
   if (c->comm_stream) cudaStreamDestroy(c->comm_stream);  // releases once its work has ended
   delete c;

@@ -46,6 +46,35 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // ---------------------------------------------------------------------------
+// flags in other GPUs' memory (peer.cu, the attention's peer epilogue)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Publish `epoch` at *flags[p] (p < nflags, flags may live in other GPUs'
+// memory) once every CTA of this grid is done with its stores. Called by
+// every thread of every CTA after its stores.
+__device__ __forceinline__ void last_cta_signal(uint32_t* counter, uint32_t* const* flags, int nflags,
+                                                uint32_t epoch) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(counter, 1u) == total - 1) {
+      *counter = 0;  // the next launch counts from zero (stream-ordered after this one)
+      __threadfence_system();
+      for (int p = 0; p < nflags; ++p) st_release_sys(flags[p], epoch);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // shared memory / mbarrier
 // ---------------------------------------------------------------------------
 // Row of a per-token modulation table [rows, 9, D] for token t. The reference

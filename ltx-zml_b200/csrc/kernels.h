@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -108,6 +109,18 @@ struct AttnArgs {
   // tiles [z n / s, (z + 1) n / s) and writes its own state at o_acc + z Tq H
   // 128, m/l + z H Tq; attention_combine merges the s states into `out`.
   int kv_splits;
+  // Output into other ranks' memory (head-parallel exchange, peer.cu): with
+  // out_tab set, output row i goes to out_tab[i / peer_rows] (a device
+  // array of pointers) at row i % peer_rows, columns out_col0 + h 128 ..,
+  // row stride ldo; `out` is unused. With sig_counter set, the last CTA to
+  // finish publishes sig_epoch at *sig_tab[p] for p < sig_n (device array).
+  void* const* out_tab;
+  int peer_rows;
+  int out_col0;
+  uint32_t* sig_counter;
+  uint32_t* const* sig_tab;
+  int sig_n;
+  uint32_t sig_epoch;
 };
 int attention_tc(const AttnArgs& a, cudaStream_t st);
 // out = (merged state of a.kv_splits splits, 1 for a ring's accumulated state) / l * gate
@@ -181,6 +194,23 @@ int dequant_split(const int8_t* q, const void* scales, int scale_bf16, int N, in
 int sp_regroup(const void* const* srcs, const int* lds, int nsrc, int T, int D, int N, int SG, void* dst,
                cudaStream_t st);
 int sp_ungroup(const void* src, int T, int D, int N, int SG, void* out, int ld_out, cudaStream_t st);
+// ---- head-parallel exchange over peer memory (peer.cu) ----
+constexpr int kMaxPeers = 8;
+struct PeerScatterArgs {
+  const __nv_bfloat16* src[3];  // q, k, v of this rank's tokens, [T, >= D], row strides ld
+  int ld[3];
+  const float* gate;            // [T, G] f32 or null
+  int G;
+  __nv_bfloat16* rx[kMaxPeers]; // per owner rank p: its receive buffer [3][N][T][D/N] (peer address)
+  float* gall[kMaxPeers];       // per rank p: its gate buffer [N T][G] (peer address)
+  uint32_t* flag[kMaxPeers];    // per rank p: the arrival flag of this rank in p's window
+  uint32_t* counter;            // this rank's CTA counter (zero between launches)
+  uint32_t epoch;
+  int N, r, T, D;
+};
+int peer_scatter(const PeerScatterArgs& a, cudaStream_t st);
+// bounded wait until flags[p] has reached `epoch` for every p != r
+int peer_wait(const uint32_t* flags, int N, int r, uint32_t epoch, uint32_t site, cudaStream_t st);
 // rows x cols f32 (row stride ld_in) -> bf16 (row stride ld_out)
 int cast_rows_f32_bf16(const float* in, int ld_in, void* out, int ld_out, int rows, int cols, cudaStream_t st);
 

@@ -89,6 +89,7 @@ def _load() -> ctypes.CDLL:
         "ltxb_comm_init": (i32, [vp, i32, i32, i32, ctypes.POINTER(vp)]),
         "ltxb_comm_free": (None, [vp]),
         "ltxb_comm_check": (i32, [vp]),
+        "ltxb_comm_peer_mapped": (i32, [vp]),
         "ltxb_comm_abort": (None, [vp]),
         "ltxb_block_workspace_bytes": (u64, [vp, vp]),
         "ltxb_ring_step": (i32, [i32, i32, i32, vp, vp, vp, vp]),
@@ -552,6 +553,11 @@ class Comm:
         buf = ctypes.create_string_buffer(uid, len(uid))
         _check(lib.ltxb_comm_init(buf, rank, nranks, device, ctypes.byref(h)))
         self.handle, self.rank, self.nranks = h, rank, nranks
+
+    def peer_mapped(self) -> bool:
+        """True when every rank mapped every other rank's memory window, so
+        the head-parallel exchange can run as stores into peer memory."""
+        return bool(lib.ltxb_comm_peer_mapped(self.handle))
 
     def free(self):
         if self.handle:

@@ -1,6 +1,7 @@
-"""Multi-GPU test of the sequence-parallel block over NCCL, with each of the
-library's exchanges (LTXB_SP): the head-parallel all-to-all (the default),
-the K/V all-gather with split-K/V attention, and the send/recv ring:
+"""Multi-GPU test of the sequence-parallel block, with each of the library's
+exchanges (LTXB_SP): the head-parallel exchange by stores into the other
+ranks' memory, the same exchange over NCCL send/recv, the K/V all-gather
+with split-K/V attention, and the send/recv ring:
 tokens split across ranks, each rank holding its slice of x / tidx / RoPE
 tables; the gathered outputs must match the f64 oracle of the whole block and
 the single-GPU run of the library. Needs >= 2 GPUs (skipped otherwise).
@@ -46,14 +47,20 @@ def _worker(rank, world, uid, grid, seed, mode, algo, q):
         part = (x[sl].contiguous(), tstab, tidx[sl].contiguous(), ctx, pts2, cos[sl].contiguous(),
                 sin[sl].contiguous())
         comm = ltxb.Comm(uid, rank, world, rank) if world > 1 else None
+        if comm is not None and algo == "peer" and not comm.peer_mapped():
+            raise RuntimeError("peer windows not mapped")
         blk = ltxb.Block(w, comm)
         out = blk.forward(*part)
-        out2 = blk.forward(*part)  # second call reuses the ring buffers
+        # later calls reuse the exchange buffers (the peer windows alternate
+        # two buffers by call parity: calls 1, 2, 3 use both, then the first again)
+        out2 = blk.forward(*part)
+        out3 = blk.forward(*part)
         torch.cuda.synchronize()
         st = ltxb.device_status()
         if comm is not None:
             comm.check()  # no error recorded on the group
-        q.put((rank, out.cpu().numpy(), bool(torch.equal(out, out2)), st, None))
+        same = bool(torch.equal(out, out2)) and bool(torch.equal(out, out3))
+        q.put((rank, out.cpu().numpy(), same, st, None))
         if comm is not None:
             comm.free()
         w.free()
@@ -92,7 +99,7 @@ def _spawn(world, target, args):
     return np.concatenate([res[r][0] for r in range(world)], axis=0)
 
 
-@pytest.mark.parametrize("algo", ["alltoall", "allgather", "ring"])
+@pytest.mark.parametrize("algo", ["peer", "alltoall", "allgather", "ring"])
 @pytest.mark.parametrize("mode,grid", [("bf16", (2, 4, 32)), ("int8", (3, 4, 16))])
 def test_sp_block_matches_single_gpu_and_oracle(mode, grid, algo):
     if torch.cuda.device_count() < 2:
@@ -107,6 +114,8 @@ def test_sp_block_matches_single_gpu_and_oracle(mode, grid, algo):
     assert ref.rel_rms(sp, want) < 5e-3
     assert ref.rel_rms(single, want) < 5e-3
     assert ref.rel_rms(sp, single) < 3e-3
+    if algo in ("peer", "alltoall"):  # every head computed as on one GPU
+        assert np.array_equal(sp, single)
 
 
 def _denoise_case():
