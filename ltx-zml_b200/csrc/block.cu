@@ -58,16 +58,19 @@ struct ltxb_weights {
 //   rx[2]         [3][N][T][D/N] bf16: q, k, v of the owned heads, all tokens
 //   orx[2]        [T][D] bf16: this rank's attention output, all heads
 //   gall[2]       [N T][G] f32: every rank's gate logits
+//   kv[2]         [S][2D] f32: the prompt K/V columns this rank computes
 struct PeerWin {
   uint8_t* local = nullptr;
   size_t bytes = 0;
   std::vector<uint8_t*> base;  // every rank's window as mapped in this process
   std::vector<char> opened;    // base[p] came from cudaIpcOpenMemHandle
-  size_t off_rx[2] = {}, off_orx[2] = {}, off_gall[2] = {};
-  int T = 0, D = 0, G = 0;     // the shapes the layout was made for
+  size_t off_rx[2] = {}, off_orx[2] = {}, off_gall[2] = {}, off_kv[2] = {};
+  int T = 0, D = 0, G = 0, S = 0;  // the shapes the layout was made for
   uint32_t epoch = 0;          // block calls through the window since it was made
 };
-constexpr int kMaxSub = 16, kWinKinds = 2 * kMaxSub;
+// flag kinds: q/k/v of sub-group g (g < kMaxSub), output of sub-group g
+// (kMaxSub + g), prompt K/V columns (kKindKv)
+constexpr int kMaxSub = 16, kKindKv = 2 * kMaxSub, kWinKinds = kKindKv + 1;
 using ltxb::kMaxPeers;
 constexpr size_t kWinCnt = (size_t)kWinKinds * kMaxPeers * 4, kWinOrx = kWinCnt + 256,
                  kWinFlago = kWinOrx + 2 * kMaxPeers * 8, kWinHdr = 4096;
@@ -611,24 +614,27 @@ static int win_setup(ltxb_comm* c, size_t bytes) {
 // Makes the window fit a block call of T tokens per rank (collective and
 // synchronous when the shapes change, otherwise free) and writes the device
 // pointer tables the kernels index.
-static int win_prepare(ltxb_comm* c, int T, int D, int G) {
+static int win_prepare(ltxb_comm* c, int T, int D, int G, int S) {
   PeerWin& W = c->win;
-  if (W.local && W.T == T && W.D == D && W.G == G) return LTXB_OK;
+  if (W.local && W.T == T && W.D == D && W.G == G && W.S == S) return LTXB_OK;
   const int N = c->nranks, r = c->rank;
   auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
-  size_t off = kWinHdr, o_rx[2], o_orx[2], o_gall[2];
+  size_t off = kWinHdr, o_rx[2], o_orx[2], o_gall[2], o_kv[2];
   for (int i = 0; i < 2; ++i) { o_rx[i] = off; off += al((size_t)3 * N * T * (D / N) * 2); }
   for (int i = 0; i < 2; ++i) { o_orx[i] = off; off += al((size_t)T * D * 2); }
   for (int i = 0; i < 2; ++i) { o_gall[i] = off; off += al((size_t)N * T * G * 4); }
+  for (int i = 0; i < 2; ++i) { o_kv[i] = off; off += al((size_t)S * 2 * D * 4); }
   if (int rc = win_setup(c, off)) return rc;
   for (int i = 0; i < 2; ++i) {
     W.off_rx[i] = o_rx[i];
     W.off_orx[i] = o_orx[i];
     W.off_gall[i] = o_gall[i];
+    W.off_kv[i] = o_kv[i];
   }
   W.T = T;
   W.D = D;
   W.G = G;
+  W.S = S;
   uint64_t orx[2][kMaxPeers] = {}, flago[kMaxSub][kMaxPeers] = {};
   for (int p = 0; p < N; ++p) {
     for (int i = 0; i < 2; ++i) orx[i][p] = reinterpret_cast<uint64_t>(W.base[p] + o_orx[i]);
@@ -661,7 +667,7 @@ static int peer_start(const ltxb_weights* w, const ltxb_config* c, const void* q
     return set_error(LTXB_EUNSUPPORTED, "peer exchange: the ranks could not map each other's memory");
   if (c->sp_size > kMaxPeers || w->H % c->sp_size)
     return set_error(LTXB_EUNSUPPORTED, "peer exchange: %d ranks, %d heads", c->sp_size, w->H);
-  if (int rc = win_prepare(cm, c->T, w->D, w->G)) return rc;
+  if (int rc = win_prepare(cm, c->T, w->D, w->G, c->S)) return rc;
   PeerWin& W = cm->win;
   const uint32_t e = ++W.epoch;
   const int par = e & 1, N = c->sp_size, r = c->sp_rank, SG = peer_subgroups(w, c);
@@ -912,33 +918,61 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
     } else {
       const Lin& L = w->kv2;
       const int parts = L.wq ? 3 : 2;
+      // With the peer exchange each rank computes 2D / N of the output
+      // columns (rows of the weight) into its window, and the ranks read
+      // each other's columns: the expansion and the weight reads shrink N-fold.
+      const bool split = sp && alg == SP_PEER && (2 * D / c->sp_size) % 128 == 0;
+      const int ncol = split ? 2 * D / c->sp_size : 2 * D, c0 = split ? c->sp_rank * ncol : 0;
+      PeerWin* W = split ? &c->comm->win : nullptr;
+      const int par = split ? (int)(W->epoch & 1) : 0;
       CK(ctx_modulate(io->ctx, S, D, w->psst, io->pts2, nullptr, b.enc32, st));
       CK(split_f32_bf16(b.enc32, S, D, parts, b.enc_split, st));
       GemmArgs g{};
       g.A = b.enc_split;
       g.lda = parts * D;
       g.M = S;
-      g.N = 2 * D;
+      g.N = ncol;
       g.K = parts * D;
       g.bn = 128;  // 64 CTAs for the 128 text tokens instead of 32
       g.epi = EPI_F32;
-      g.bias = L.b;
-      g.out = b.kv2_32;
+      g.bias = L.b ? static_cast<const __nv_bfloat16*>(L.b) + c0 : nullptr;
+      g.out = split ? reinterpret_cast<float*>(W->local + W->off_kv[par]) + c0 : b.kv2_32;
       g.ldo = 2 * D;
       if (L.wq) {
-        if ((size_t)2 * D * 2 * D > b.deq_elems)
+        if ((size_t)ncol * 2 * D > b.deq_elems)
           return set_error(LTXB_EINVAL, "prompt K/V: split expansion exceeds the expansion buffer");
         g.B = b.deq;
         g.ldb = 2 * D;
         g.b_kwrap = 2 * D;
         CK(gemm_check(g, nullptr));
-        CK(dequant_split(L.wq, L.sc, L.sc_bf16, 2 * D, D, b.deq, st));
+        const size_t sc_off = (size_t)c0 * (D / 128) * (L.sc_bf16 ? 2 : 4);
+        CK(dequant_split(L.wq + (size_t)c0 * D, static_cast<const uint8_t*>(L.sc) + sc_off, L.sc_bf16, ncol, D, b.deq,
+                         st));
       } else {
-        g.B = L.w;
+        g.B = static_cast<const __nv_bfloat16*>(L.w) + (size_t)c0 * D;
         g.ldb = D;
         g.b_kwrap = D;
       }
       CK(gemm_tc(g, st));
+      if (split) {
+        const int N = c->sp_size, r = c->sp_rank;
+        PeerFlags f{};
+        PeerGatherArgs ga{};
+        for (int p = 0; p < N; ++p) {
+          f.p[p] = reinterpret_cast<uint32_t*>(W->base[p] + win_flag(kKindKv, r));
+          ga.src[p] = reinterpret_cast<const float*>(W->base[p] + W->off_kv[par]);
+        }
+        f.n = N;
+        CK(peer_signal(f, W->epoch, st));
+        CK(peer_wait(reinterpret_cast<const uint32_t*>(W->local + win_flag(kKindKv, 0)), 1, N, r, W->epoch, 0x303,
+                     st));
+        ga.dst = b.kv2_32;
+        ga.rows = S;
+        ga.cols = 2 * D;
+        ga.slice = ncol;
+        ga.ld_src = ga.ld_dst = 2 * D;
+        CK(peer_gather_cols(ga, st));
+      }
       CK(qk_norm_rope_f32(b.kv2_32, 2 * D, w->kn2, nullptr, nullptr, S, D, nullptr, st, b.k2));
       CK(cast_rows_f32_bf16(b.kv2_32 + D, 2 * D, col(b.kv2, D), 2 * D, S, D, st));
     }

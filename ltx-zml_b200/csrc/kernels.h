@@ -210,6 +210,20 @@ struct PeerScatterArgs {
   int N, r, T, D;
 };
 int peer_scatter(const PeerScatterArgs& a, cudaStream_t st);
+// flags in other ranks' memory, raised together
+struct PeerFlags {
+  uint32_t* p[kMaxPeers];
+  int n;
+};
+int peer_signal(const PeerFlags& f, uint32_t epoch, cudaStream_t st);
+// dst [rows, cols] f32 (row stride ld_dst) from column slices of `slice`
+// columns, slice p read from src[p] (row stride ld_src, peer addresses)
+struct PeerGatherArgs {
+  const float* src[kMaxPeers];
+  float* dst;
+  int rows, cols, slice, ld_src, ld_dst;
+};
+int peer_gather_cols(const PeerGatherArgs& a, cudaStream_t st);
 // bounded wait until flags[k kMaxPeers + p] has reached `epoch` for every
 // k < nkinds and p != r
 int peer_wait(const uint32_t* flags, int nkinds, int N, int r, uint32_t epoch, uint32_t site, cudaStream_t st);

@@ -100,6 +100,45 @@ __global__ void peer_wait_kernel(const uint32_t* flags, int nkinds, int N, int r
   __threadfence_system();
 }
 
+// Publish `epoch` at every flag once this stream's earlier work is done
+// (what that work wrote is visible to whoever reads the flag).
+__global__ void peer_signal_kernel(const PeerFlags f, uint32_t epoch) {
+  __threadfence_system();
+  if (threadIdx.x < f.n) st_release_sys(f.p[threadIdx.x], epoch);
+}
+
+// dst[i, c] = src[c / slice][i, c] for a [rows, cols] f32 matrix whose
+// column slices live in different ranks' memory (same row stride ld_src).
+__global__ void peer_gather_cols_kernel(const PeerGatherArgs a) {
+  const int c4 = a.cols / 4, n = a.rows * c4;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int row = i / c4, c = (i % c4) * 4, p = c / a.slice;
+    *reinterpret_cast<float4*>(a.dst + (size_t)row * a.ld_dst + c) =
+        *reinterpret_cast<const float4*>(a.src[p] + (size_t)row * a.ld_src + c);
+  }
+}
+
+int peer_signal(const PeerFlags& f, uint32_t epoch, cudaStream_t st) {
+  if (f.n < 1 || f.n > kMaxPeers) return set_error(LTXB_EINVAL, "peer signal: %d flags", f.n);
+  peer_signal_kernel<<<1, 32, 0, st>>>(f, epoch);
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "peer signal");
+}
+
+int peer_gather_cols(const PeerGatherArgs& a, cudaStream_t st) {
+  if (a.rows < 1 || a.cols % 4 || a.slice % 4 || a.slice < 4 || a.cols > a.slice * kMaxPeers || a.ld_src % 4 ||
+      a.ld_dst % 4)
+    return set_error(LTXB_EINVAL, "peer gather: %d x %d, slice %d", a.rows, a.cols, a.slice);
+  const int n = a.rows * (a.cols / 4);
+  int grid = (n + 255) / 256;
+  if (grid > 2 * sm_count()) grid = 2 * sm_count();
+  peer_gather_cols_kernel<<<grid, 256, 0, st>>>(a);
+  launched();
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "peer gather");
+}
+
 int peer_scatter(const PeerScatterArgs& a, cudaStream_t st) {
   if (a.N < 2 || a.N > kMaxPeers || a.r < 0 || a.r >= a.N || a.T < 1 || a.D % a.N || (a.D / a.N) % 8 || a.G % 4 ||
       a.c0 < 0 || a.cw <= 0 || a.c0 % 8 || a.cw % 8 || a.c0 + a.cw > a.D / a.N)
