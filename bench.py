@@ -3,9 +3,9 @@
 (22x32x40 latent grid, D 4096, 32x128 heads, FFN 16384,
 128 text tokens, int8 grouped-128 weights with bf16 scales for the q/k/v,
 output and FFN projections), on 1..N B200s of one node with the tokens
-sharded across ranks (sequence-parallel self-attention: a head-parallel
-all-to-all of q/k/v over NVLink with NCCL, each rank attending its H/N heads
-over all tokens).
+sharded across ranks (sequence-parallel self-attention: head-parallel, each
+rank attending its H/N heads over all tokens, with q/k/v and the attention
+rows stored over NVLink straight into the other GPUs' memory).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -40,7 +40,7 @@ import torch  # noqa: E402
 T_TOTAL, GRID, S, D, FF, H = 28160, (22, 32, 40), 128, 4096, 16384, 32
 METRIC = "dit_block_tflops_28k_int8w"
 # the library's default sequence-parallel exchange (LTXB_SP unset)
-SP_DEFAULT = "alltoall"
+SP_DEFAULT = "peer"
 # token counts of the CPU samples (latent grids with T % 1024 == 0, so the
 # restated whileSdpa runs its production chunk of 1024 on every sample)
 CPU_SAMPLE_GRIDS = ((8, 8, 16), (16, 8, 16), (12, 16, 16), (16, 16, 16))

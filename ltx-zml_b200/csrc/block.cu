@@ -46,36 +46,27 @@ struct ltxb_weights {
 // Peer window: device memory of this rank that every other rank of the
 // communicator has mapped (CUDA IPC), for the head-parallel exchange over
 // peer memory (peer.cu). Offsets are identical on every rank:
-//   [0, kWinHdr)  header: arrival flags [kWinKinds][kMaxPeers] u32 at 0
-//                 (kind g < kMaxSub: q/k/v of head sub-group g, with the
-//                 gates in sub-group 0; kind kMaxSub + g: the attention
-//                 output of sub-group g; entry p written by rank p), CTA
-//                 counters [2] at kWinCnt, and the device pointer tables the
-//                 kernels index, as this process maps them: at kWinOrx every
-//                 rank's output buffer [2 parities][kMaxPeers], at kWinFlago
-//                 this rank's output flag of sub-group g in every window
-//                 [kMaxSub][kMaxPeers]
+//   [0, kWinHdr)  header: arrival flags [2 kinds][kMaxPeers] u32 at 0 (kind
+//                 0: q/k/v and gates, 1: attention output; entry p written
+//                 by rank p), CTA counters [2] at 256, and from kWinTab the
+//                 device pointer tables the kernels index, as this process
+//                 maps them: [table][2 parities][kMaxPeers] (orx: every
+//                 rank's output buffer; flago: this rank's kind-1 flag in
+//                 every window)
 //   rx[2]         [3][N][T][D/N] bf16: q, k, v of the owned heads, all tokens
 //   orx[2]        [T][D] bf16: this rank's attention output, all heads
 //   gall[2]       [N T][G] f32: every rank's gate logits
-//   kv[2]         [S][2D] f32: the prompt K/V columns this rank computes
 struct PeerWin {
   uint8_t* local = nullptr;
   size_t bytes = 0;
   std::vector<uint8_t*> base;  // every rank's window as mapped in this process
   std::vector<char> opened;    // base[p] came from cudaIpcOpenMemHandle
-  size_t off_rx[2] = {}, off_orx[2] = {}, off_gall[2] = {}, off_kv[2] = {};
-  int T = 0, D = 0, G = 0, S = 0;  // the shapes the layout was made for
+  size_t off_rx[2] = {}, off_orx[2] = {}, off_gall[2] = {};
+  int T = 0, D = 0, G = 0;     // the shapes the layout was made for
   uint32_t epoch = 0;          // block calls through the window since it was made
 };
-// flag kinds: q/k/v of sub-group g (g < kMaxSub), output of sub-group g
-// (kMaxSub + g), prompt K/V columns (kKindKv)
-constexpr int kMaxSub = 16, kKindKv = 2 * kMaxSub, kWinKinds = kKindKv + 1;
-using ltxb::kMaxPeers;
-constexpr size_t kWinCnt = (size_t)kWinKinds * kMaxPeers * 4, kWinOrx = kWinCnt + 256,
-                 kWinFlago = kWinOrx + 2 * kMaxPeers * 8, kWinHdr = 4096;
-static_assert(kWinFlago + (size_t)kMaxSub * kMaxPeers * 8 <= kWinHdr, "peer window header");
-static size_t win_flag(int kind, int src) { return ((size_t)kind * kMaxPeers + src) * 4; }
+constexpr size_t kWinHdr = 4096, kWinTab = 1024;
+enum WinTable { TAB_ORX = 0, TAB_FLAGO = 1 };
 
 struct ltxb_comm {
   ncclComm_t nccl = nullptr;
@@ -152,9 +143,9 @@ constexpr int kModTableRows = 64;
 //   SP_RING      K/V shards passed around a ring (LTXB_SP=ring or
 //                LTXB_SP_RING=1), kept for comparison
 //   SP_PEER      head-parallel like SP_ALLTOALL, the exchange written as
-//                stores into the other ranks' memory (peer.cu); needs every
-//                rank to have mapped every other rank's window
-//                (LTXB_SP=peer)
+//                stores into the other ranks' memory (peer.cu): the default
+//                when the heads divide evenly and every rank mapped every
+//                other rank's window (LTXB_SP=alltoall forces the NCCL form)
 enum SpAlgo { SP_ALLTOALL = 0, SP_ALLGATHER = 1, SP_RING = 2, SP_PEER = 3 };
 static int sp_env_algo() {
   static const int a = [] {
@@ -175,7 +166,9 @@ static SpAlgo sp_algo(const ltxb_weights* w, const ltxb_config* c) {
   const int e = sp_env_algo();
   if (e == SP_RING || e == SP_ALLGATHER) return static_cast<SpAlgo>(e);
   if (e == SP_PEER) return SP_PEER;  // the forward call reports it if the windows are missing
-  return a2a_ok ? SP_ALLTOALL : SP_ALLGATHER;
+  if (e == SP_ALLTOALL) return a2a_ok ? SP_ALLTOALL : SP_ALLGATHER;
+  const bool peer_ok = a2a_ok && n <= kMaxPeers && c->comm && c->comm->peer_ok;
+  return peer_ok ? SP_PEER : a2a_ok ? SP_ALLTOALL : SP_ALLGATHER;
 }
 static bool sp_use_ring(const ltxb_weights* w, const ltxb_config* c) { return sp_algo(w, c) == SP_RING; }
 // K/V splits of the gathered attention (1 for the ring, whose steps merge
@@ -614,52 +607,39 @@ static int win_setup(ltxb_comm* c, size_t bytes) {
 // Makes the window fit a block call of T tokens per rank (collective and
 // synchronous when the shapes change, otherwise free) and writes the device
 // pointer tables the kernels index.
-static int win_prepare(ltxb_comm* c, int T, int D, int G, int S) {
+static int win_prepare(ltxb_comm* c, int T, int D, int G) {
   PeerWin& W = c->win;
-  if (W.local && W.T == T && W.D == D && W.G == G && W.S == S) return LTXB_OK;
+  if (W.local && W.T == T && W.D == D && W.G == G) return LTXB_OK;
   const int N = c->nranks, r = c->rank;
   auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
-  size_t off = kWinHdr, o_rx[2], o_orx[2], o_gall[2], o_kv[2];
+  size_t off = kWinHdr, o_rx[2], o_orx[2], o_gall[2];
   for (int i = 0; i < 2; ++i) { o_rx[i] = off; off += al((size_t)3 * N * T * (D / N) * 2); }
   for (int i = 0; i < 2; ++i) { o_orx[i] = off; off += al((size_t)T * D * 2); }
   for (int i = 0; i < 2; ++i) { o_gall[i] = off; off += al((size_t)N * T * G * 4); }
-  for (int i = 0; i < 2; ++i) { o_kv[i] = off; off += al((size_t)S * 2 * D * 4); }
   if (int rc = win_setup(c, off)) return rc;
   for (int i = 0; i < 2; ++i) {
     W.off_rx[i] = o_rx[i];
     W.off_orx[i] = o_orx[i];
     W.off_gall[i] = o_gall[i];
-    W.off_kv[i] = o_kv[i];
   }
   W.T = T;
   W.D = D;
   W.G = G;
-  W.S = S;
-  uint64_t orx[2][kMaxPeers] = {}, flago[kMaxSub][kMaxPeers] = {};
-  for (int p = 0; p < N; ++p) {
-    for (int i = 0; i < 2; ++i) orx[i][p] = reinterpret_cast<uint64_t>(W.base[p] + o_orx[i]);
-    for (int g = 0; g < kMaxSub; ++g) flago[g][p] = reinterpret_cast<uint64_t>(W.base[p] + win_flag(kMaxSub + g, r));
-  }
-  if (cudaMemcpyAsync(W.local + kWinOrx, orx, sizeof(orx), cudaMemcpyHostToDevice, c->comm_stream) != cudaSuccess ||
-      cudaMemcpyAsync(W.local + kWinFlago, flago, sizeof(flago), cudaMemcpyHostToDevice, c->comm_stream) !=
-          cudaSuccess ||
+  uint64_t tab[2][2][kMaxPeers] = {};
+  for (int i = 0; i < 2; ++i)
+    for (int p = 0; p < N; ++p) {
+      tab[TAB_ORX][i][p] = reinterpret_cast<uint64_t>(W.base[p] + o_orx[i]);
+      tab[TAB_FLAGO][i][p] = reinterpret_cast<uint64_t>(W.base[p] + (size_t)(1 * kMaxPeers + r) * 4);
+    }
+  if (cudaMemcpyAsync(W.local + kWinTab, tab, sizeof(tab), cudaMemcpyHostToDevice, c->comm_stream) != cudaSuccess ||
       cudaStreamSynchronize(c->comm_stream) != cudaSuccess)
     return set_error(LTXB_ECUDA, "peer window: tables");
   return LTXB_OK;
 }
 
-// Head sub-groups of the peer exchange: sub-group g's q/k/v travel and are
-// attended on their own, so that its attention overlaps the transfer of the
-// later sub-groups (4 heads each when the owned heads allow: 4 x 110
-// query-tile pairs at 28,160 tokens fill whole waves on 148 SMs).
-static int peer_subgroups(const ltxb_weights* w, const ltxb_config* c) {
-  const int hn = w->H / c->sp_size;
-  return hn % 4 == 0 && hn / 4 <= kMaxSub ? hn / 4 : 1;
-}
-
 // SP_PEER, step 1 (before the prompt K/V): this rank's q, k, v and gate
-// logits into the owners' windows, sub-group by sub-group on the comm
-// stream; returns the epoch of this call.
+// logits into the owners' windows, on the comm stream; returns the epoch of
+// this call.
 static int peer_start(const ltxb_weights* w, const ltxb_config* c, const void* q, const void* k, const void* v,
                       int ldv, const float* gate, cudaStream_t st, uint32_t* epoch) {
   ltxb_comm* cm = c->comm;
@@ -667,82 +647,72 @@ static int peer_start(const ltxb_weights* w, const ltxb_config* c, const void* q
     return set_error(LTXB_EUNSUPPORTED, "peer exchange: the ranks could not map each other's memory");
   if (c->sp_size > kMaxPeers || w->H % c->sp_size)
     return set_error(LTXB_EUNSUPPORTED, "peer exchange: %d ranks, %d heads", c->sp_size, w->H);
-  if (int rc = win_prepare(cm, c->T, w->D, w->G, c->S)) return rc;
+  if (int rc = win_prepare(cm, c->T, w->D, w->G)) return rc;
   PeerWin& W = cm->win;
   const uint32_t e = ++W.epoch;
-  const int par = e & 1, N = c->sp_size, r = c->sp_rank, SG = peer_subgroups(w, c);
-  const int Dg = w->D / N / SG;
-  if ((int)cm->ev.size() < 1 + SG) return set_error(LTXB_EINVAL, "sp: communicator event pool too small");
+  const int par = e & 1, N = c->sp_size, r = c->sp_rank;
+  PeerScatterArgs a{};
+  a.src[0] = static_cast<const __nv_bfloat16*>(q);
+  a.src[1] = static_cast<const __nv_bfloat16*>(k);
+  a.src[2] = static_cast<const __nv_bfloat16*>(v);
+  a.ld[0] = a.ld[1] = w->D;
+  a.ld[2] = ldv;
+  a.gate = gate;
+  a.G = w->G;
+  for (int p = 0; p < N; ++p) {
+    a.rx[p] = reinterpret_cast<__nv_bfloat16*>(W.base[p] + W.off_rx[par]);
+    a.gall[p] = reinterpret_cast<float*>(W.base[p] + W.off_gall[par]);
+    a.flag[p] = reinterpret_cast<uint32_t*>(W.base[p] + (size_t)(0 * kMaxPeers + r) * 4);
+  }
+  a.counter = reinterpret_cast<uint32_t*>(W.local + 256);
+  a.epoch = e;
+  a.N = N;
+  a.r = r;
+  a.T = c->T;
+  a.D = w->D;
   cudaEventRecord(cm->ev[0], st);
   cudaStreamWaitEvent(cm->comm_stream, cm->ev[0], 0);
-  for (int g = 0; g < SG; ++g) {
-    PeerScatterArgs a{};
-    a.src[0] = static_cast<const __nv_bfloat16*>(q);
-    a.src[1] = static_cast<const __nv_bfloat16*>(k);
-    a.src[2] = static_cast<const __nv_bfloat16*>(v);
-    a.ld[0] = a.ld[1] = w->D;
-    a.ld[2] = ldv;
-    a.c0 = g * Dg;
-    a.cw = Dg;
-    a.gate = g == 0 ? gate : nullptr;
-    a.G = w->G;
-    for (int p = 0; p < N; ++p) {
-      a.rx[p] = reinterpret_cast<__nv_bfloat16*>(W.base[p] + W.off_rx[par]);
-      a.gall[p] = reinterpret_cast<float*>(W.base[p] + W.off_gall[par]);
-      a.flag[p] = reinterpret_cast<uint32_t*>(W.base[p] + win_flag(g, r));
-    }
-    a.counter = reinterpret_cast<uint32_t*>(W.local + kWinCnt);
-    a.epoch = e;
-    a.N = N;
-    a.r = r;
-    a.T = c->T;
-    a.D = w->D;
-    if (int rc = peer_scatter(a, cm->comm_stream)) return rc;
-    cudaEventRecord(cm->ev[1 + g], cm->comm_stream);
-  }
+  if (int rc = peer_scatter(a, cm->comm_stream)) return rc;
+  cudaEventRecord(cm->ev[1], cm->comm_stream);
   *epoch = e;
   return LTXB_OK;
 }
 
-// SP_PEER, step 2: per sub-group, wait for every rank's q/k/v and attend all
-// N T tokens of its heads with the output rows stored straight into their
-// ranks' windows; then wait for every rank's output rows. Returns this
-// rank's [T, D] attention output (in its window).
+// SP_PEER, step 2: wait for every rank's q/k/v, attend all N T tokens of the
+// owned heads with the output rows stored straight into their ranks'
+// windows, wait for every rank's output rows. Returns this rank's [T, D]
+// attention output (in its window).
 static int peer_finish(const ltxb_weights* w, const ltxb_config* c, uint32_t e, bool gated, cudaStream_t st,
                        void** o_out) {
   ltxb_comm* cm = c->comm;
   PeerWin& W = cm->win;
   const int par = e & 1, N = c->sp_size, r = c->sp_rank, T = c->T, D = w->D, Dn = D / N;
-  const int SG = peer_subgroups(w, c), hg = w->H / N / SG, Dg = Dn / SG;
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(W.local);
+  cudaStreamWaitEvent(st, cm->ev[1], 0);  // this rank's own slice is written by its scatter
+  if (int rc = peer_wait(flags, N, r, e, 0x301, st)) return rc;
   const uint8_t* rx = W.local + W.off_rx[par];
   const size_t blk = (size_t)N * T * Dn * 2;
-  for (int g = 0; g < SG; ++g) {
-    cudaStreamWaitEvent(st, cm->ev[1 + g], 0);  // this rank's own slice is written by its scatter
-    if (int rc = peer_wait(flags + win_flag(g, 0) / 4, 1, N, r, e, 0x301, st)) return rc;
-    AttnArgs a{};
-    a.q = rx + (size_t)g * Dg * 2;
-    a.k = rx + blk + (size_t)g * Dg * 2;
-    a.v = rx + 2 * blk + (size_t)g * Dg * 2;
-    a.ldq = a.ldk = a.ldv = Dn;
-    a.gate = gated ? reinterpret_cast<const float*>(W.local + W.off_gall[par]) + (size_t)r * (w->H / N) + g * hg
-                   : nullptr;
-    a.ldg = w->G;
-    a.Tq = N * T;
-    a.Tkv = N * T;
-    a.H = hg;
-    a.scale = 0.08838834764831845f;
-    a.ldo = D;
-    a.out_tab = reinterpret_cast<void* const*>(W.local + kWinOrx + (size_t)par * kMaxPeers * 8);
-    a.peer_rows = T;
-    a.out_col0 = r * Dn + g * Dg;
-    a.sig_counter = reinterpret_cast<uint32_t*>(W.local + kWinCnt + 4);
-    a.sig_tab = reinterpret_cast<uint32_t* const*>(W.local + kWinFlago + (size_t)g * kMaxPeers * 8);
-    a.sig_n = N;
-    a.sig_epoch = e;
-    if (int rc = attention_tc(a, st)) return rc;
-  }
-  if (int rc = peer_wait(flags + win_flag(kMaxSub, 0) / 4, SG, N, r, e, 0x302, st)) return rc;
+  AttnArgs a{};
+  a.q = rx;
+  a.k = rx + blk;
+  a.v = rx + 2 * blk;
+  a.ldq = a.ldk = a.ldv = Dn;
+  a.gate = gated ? reinterpret_cast<const float*>(W.local + W.off_gall[par]) + (size_t)r * (w->H / N) : nullptr;
+  a.ldg = w->G;
+  a.Tq = N * T;
+  a.Tkv = N * T;
+  a.H = w->H / N;
+  a.scale = 0.08838834764831845f;
+  a.ldo = D;
+  a.out_tab = reinterpret_cast<void* const*>(W.local + kWinTab + (size_t)(TAB_ORX * 2 + par) * kMaxPeers * 8);
+  a.peer_rows = T;
+  a.out_col0 = r * Dn;
+  a.sig_counter = reinterpret_cast<uint32_t*>(W.local + 256 + 4);
+  a.sig_tab = reinterpret_cast<uint32_t* const*>(W.local + kWinTab + (size_t)(TAB_FLAGO * 2 + par) * kMaxPeers * 8);
+  a.sig_n = N;
+  a.sig_epoch = e;
+  if (int rc = attention_tc(a, st)) return rc;
+  if (int rc = peer_wait(flags + kMaxPeers, N, r, e, 0x302, st)) return rc;
   *o_out = W.local + W.off_orx[par];
   return LTXB_OK;
 }
@@ -918,61 +888,33 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
     } else {
       const Lin& L = w->kv2;
       const int parts = L.wq ? 3 : 2;
-      // With the peer exchange each rank computes 2D / N of the output
-      // columns (rows of the weight) into its window, and the ranks read
-      // each other's columns: the expansion and the weight reads shrink N-fold.
-      const bool split = sp && alg == SP_PEER && (2 * D / c->sp_size) % 128 == 0;
-      const int ncol = split ? 2 * D / c->sp_size : 2 * D, c0 = split ? c->sp_rank * ncol : 0;
-      PeerWin* W = split ? &c->comm->win : nullptr;
-      const int par = split ? (int)(W->epoch & 1) : 0;
       CK(ctx_modulate(io->ctx, S, D, w->psst, io->pts2, nullptr, b.enc32, st));
       CK(split_f32_bf16(b.enc32, S, D, parts, b.enc_split, st));
       GemmArgs g{};
       g.A = b.enc_split;
       g.lda = parts * D;
       g.M = S;
-      g.N = ncol;
+      g.N = 2 * D;
       g.K = parts * D;
       g.bn = 128;  // 64 CTAs for the 128 text tokens instead of 32
       g.epi = EPI_F32;
-      g.bias = L.b ? static_cast<const __nv_bfloat16*>(L.b) + c0 : nullptr;
-      g.out = split ? reinterpret_cast<float*>(W->local + W->off_kv[par]) + c0 : b.kv2_32;
+      g.bias = L.b;
+      g.out = b.kv2_32;
       g.ldo = 2 * D;
       if (L.wq) {
-        if ((size_t)ncol * 2 * D > b.deq_elems)
+        if ((size_t)2 * D * 2 * D > b.deq_elems)
           return set_error(LTXB_EINVAL, "prompt K/V: split expansion exceeds the expansion buffer");
         g.B = b.deq;
         g.ldb = 2 * D;
         g.b_kwrap = 2 * D;
         CK(gemm_check(g, nullptr));
-        const size_t sc_off = (size_t)c0 * (D / 128) * (L.sc_bf16 ? 2 : 4);
-        CK(dequant_split(L.wq + (size_t)c0 * D, static_cast<const uint8_t*>(L.sc) + sc_off, L.sc_bf16, ncol, D, b.deq,
-                         st));
+        CK(dequant_split(L.wq, L.sc, L.sc_bf16, 2 * D, D, b.deq, st));
       } else {
-        g.B = static_cast<const __nv_bfloat16*>(L.w) + (size_t)c0 * D;
+        g.B = L.w;
         g.ldb = D;
         g.b_kwrap = D;
       }
       CK(gemm_tc(g, st));
-      if (split) {
-        const int N = c->sp_size, r = c->sp_rank;
-        PeerFlags f{};
-        PeerGatherArgs ga{};
-        for (int p = 0; p < N; ++p) {
-          f.p[p] = reinterpret_cast<uint32_t*>(W->base[p] + win_flag(kKindKv, r));
-          ga.src[p] = reinterpret_cast<const float*>(W->base[p] + W->off_kv[par]);
-        }
-        f.n = N;
-        CK(peer_signal(f, W->epoch, st));
-        CK(peer_wait(reinterpret_cast<const uint32_t*>(W->local + win_flag(kKindKv, 0)), 1, N, r, W->epoch, 0x303,
-                     st));
-        ga.dst = b.kv2_32;
-        ga.rows = S;
-        ga.cols = 2 * D;
-        ga.slice = ncol;
-        ga.ld_src = ga.ld_dst = 2 * D;
-        CK(peer_gather_cols(ga, st));
-      }
       CK(qk_norm_rope_f32(b.kv2_32, 2 * D, w->kn2, nullptr, nullptr, S, D, nullptr, st, b.k2));
       CK(cast_rows_f32_bf16(b.kv2_32 + D, 2 * D, col(b.kv2, D), 2 * D, S, D, st));
     }

@@ -199,7 +199,6 @@ constexpr int kMaxPeers = 8;
 struct PeerScatterArgs {
   const __nv_bfloat16* src[3];  // q, k, v of this rank's tokens, [T, >= D], row strides ld
   int ld[3];
-  int c0, cw;                   // columns [c0, c0 + cw) of every owner's D/N slice (multiples of 8)
   const float* gate;            // [T, G] f32 or null
   int G;
   __nv_bfloat16* rx[kMaxPeers]; // per owner rank p: its receive buffer [3][N][T][D/N] (peer address)
@@ -210,23 +209,8 @@ struct PeerScatterArgs {
   int N, r, T, D;
 };
 int peer_scatter(const PeerScatterArgs& a, cudaStream_t st);
-// flags in other ranks' memory, raised together
-struct PeerFlags {
-  uint32_t* p[kMaxPeers];
-  int n;
-};
-int peer_signal(const PeerFlags& f, uint32_t epoch, cudaStream_t st);
-// dst [rows, cols] f32 (row stride ld_dst) from column slices of `slice`
-// columns, slice p read from src[p] (row stride ld_src, peer addresses)
-struct PeerGatherArgs {
-  const float* src[kMaxPeers];
-  float* dst;
-  int rows, cols, slice, ld_src, ld_dst;
-};
-int peer_gather_cols(const PeerGatherArgs& a, cudaStream_t st);
-// bounded wait until flags[k kMaxPeers + p] has reached `epoch` for every
-// k < nkinds and p != r
-int peer_wait(const uint32_t* flags, int nkinds, int N, int r, uint32_t epoch, uint32_t site, cudaStream_t st);
+// bounded wait until flags[p] has reached `epoch` for every p != r
+int peer_wait(const uint32_t* flags, int N, int r, uint32_t epoch, uint32_t site, cudaStream_t st);
 // rows x cols f32 (row stride ld_in) -> bf16 (row stride ld_out)
 int cast_rows_f32_bf16(const float* in, int ld_in, void* out, int ld_out, int rows, int cols, cudaStream_t st);
 

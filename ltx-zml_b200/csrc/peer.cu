@@ -36,11 +36,8 @@
 
 namespace ltxb {
 
-// At most 40 registers (6 CTAs per SM by register count), so that one CTA fits
-// beside a resident attention CTA (576 threads x 96 registers) and the
-// transfer of a later sub-group overlaps the attention of an earlier one.
-__global__ void __launch_bounds__(256, 6) peer_scatter_kernel(const PeerScatterArgs a) {
-  const int Dn = a.D / a.N, c16 = a.cw / 8;  // 16-byte units per row slice
+__global__ void __launch_bounds__(256) peer_scatter_kernel(const PeerScatterArgs a) {
+  const int Dn = a.D / a.N, c16 = Dn / 8;  // 16-byte units per row slice
   const int tid = blockIdx.x * blockDim.x + threadIdx.x, nthr = gridDim.x * blockDim.x;
   // q / k / v: 16-byte units of the (tensor, owner, token) row slices of Dn
   // columns, consecutive threads on consecutive units of a slice; four units
@@ -57,8 +54,8 @@ __global__ void __launch_bounds__(256, 6) peer_scatter_kernel(const PeerScatterA
       if (u < units) {
         const int c = u % c16, row = u / c16;
         const int t = row % a.T, xp = row / a.T, p = xp % a.N, x = xp / a.N;
-        v[j] = reinterpret_cast<const uint4*>(a.src[x] + (size_t)t * a.ld[x] + (size_t)p * Dn + a.c0)[c];
-        d[j] = reinterpret_cast<uint4*>(a.rx[p] + (((size_t)x * a.N + a.r) * a.T + t) * Dn + a.c0) + c;
+        v[j] = reinterpret_cast<const uint4*>(a.src[x] + (size_t)t * a.ld[x] + (size_t)p * Dn)[c];
+        d[j] = reinterpret_cast<uint4*>(a.rx[p] + (((size_t)x * a.N + a.r) * a.T + t) * Dn) + c;
       }
     }
 #pragma unroll
@@ -77,16 +74,15 @@ __global__ void __launch_bounds__(256, 6) peer_scatter_kernel(const PeerScatterA
   last_cta_signal(a.counter, a.flag, a.N, a.epoch);
 }
 
-// Wait until every other rank has published `epoch` in flags[k kMaxPeers
-// + p] for k < nkinds (this rank's window). Bounded: after kWaitLimitNs the
-// site is recorded in the device status word and the kernel returns.
-__global__ void peer_wait_kernel(const uint32_t* flags, int nkinds, int N, int r, uint32_t epoch, uint32_t site) {
-  const int p = threadIdx.x % kMaxPeers, k = threadIdx.x / kMaxPeers;
-  if (p < N && p != r && k < nkinds) {
-    const uint32_t* f = flags + (size_t)k * kMaxPeers + p;
+// Wait until every other rank has published `epoch` in flags[p] (this
+// rank's window). Bounded: after kWaitLimitNs the site is recorded in the
+// device status word and the kernel returns.
+__global__ void peer_wait_kernel(const uint32_t* flags, int N, int r, uint32_t epoch, uint32_t site) {
+  const int p = threadIdx.x;
+  if (p < N && p != r) {
     const uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
-    while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+    while ((int)(ld_acquire_sys(flags + p) - epoch) < 0) {
       if ((++spins & 63u) == 0) {
         if (*(volatile uint32_t*)&g_status != 0u) break;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -100,51 +96,10 @@ __global__ void peer_wait_kernel(const uint32_t* flags, int nkinds, int N, int r
   __threadfence_system();
 }
 
-// Publish `epoch` at every flag once this stream's earlier work is done
-// (what that work wrote is visible to whoever reads the flag).
-__global__ void peer_signal_kernel(const PeerFlags f, uint32_t epoch) {
-  __threadfence_system();
-  if (threadIdx.x < f.n) st_release_sys(f.p[threadIdx.x], epoch);
-}
-
-// dst[i, c] = src[c / slice][i, c] for a [rows, cols] f32 matrix whose
-// column slices live in different ranks' memory (same row stride ld_src).
-__global__ void peer_gather_cols_kernel(const PeerGatherArgs a) {
-  const int c4 = a.cols / 4, n = a.rows * c4;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int row = i / c4, c = (i % c4) * 4, p = c / a.slice;
-    *reinterpret_cast<float4*>(a.dst + (size_t)row * a.ld_dst + c) =
-        *reinterpret_cast<const float4*>(a.src[p] + (size_t)row * a.ld_src + c);
-  }
-}
-
-int peer_signal(const PeerFlags& f, uint32_t epoch, cudaStream_t st) {
-  if (f.n < 1 || f.n > kMaxPeers) return set_error(LTXB_EINVAL, "peer signal: %d flags", f.n);
-  peer_signal_kernel<<<1, 32, 0, st>>>(f, epoch);
-  launched();
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "peer signal");
-}
-
-int peer_gather_cols(const PeerGatherArgs& a, cudaStream_t st) {
-  if (a.rows < 1 || a.cols % 4 || a.slice % 4 || a.slice < 4 || a.cols > a.slice * kMaxPeers || a.ld_src % 4 ||
-      a.ld_dst % 4)
-    return set_error(LTXB_EINVAL, "peer gather: %d x %d, slice %d", a.rows, a.cols, a.slice);
-  const int n = a.rows * (a.cols / 4);
-  int grid = (n + 255) / 256;
-  if (grid > 2 * sm_count()) grid = 2 * sm_count();
-  peer_gather_cols_kernel<<<grid, 256, 0, st>>>(a);
-  launched();
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "peer gather");
-}
-
 int peer_scatter(const PeerScatterArgs& a, cudaStream_t st) {
-  if (a.N < 2 || a.N > kMaxPeers || a.r < 0 || a.r >= a.N || a.T < 1 || a.D % a.N || (a.D / a.N) % 8 || a.G % 4 ||
-      a.c0 < 0 || a.cw <= 0 || a.c0 % 8 || a.cw % 8 || a.c0 + a.cw > a.D / a.N)
-    return set_error(LTXB_EINVAL, "peer scatter: %d ranks, T %d, D %d, G %d, columns %d + %d", a.N, a.T, a.D, a.G,
-                     a.c0, a.cw);
-  if ((size_t)3 * a.N * a.T * (a.cw / 8) + (size_t)4 * sm_count() * 256 >= (1u << 31) ||
+  if (a.N < 2 || a.N > kMaxPeers || a.r < 0 || a.r >= a.N || a.T < 1 || a.D % a.N || (a.D / a.N) % 8 || a.G % 4)
+    return set_error(LTXB_EINVAL, "peer scatter: %d ranks, T %d, D %d, G %d", a.N, a.T, a.D, a.G);
+  if ((size_t)3 * a.N * a.T * (a.D / a.N / 8) + (size_t)4 * sm_count() * 256 >= (1u << 31) ||
       (size_t)a.N * a.T * (a.G / 4) + (size_t)sm_count() * 256 >= (1u << 31))
     return set_error(LTXB_EINVAL, "peer scatter: too many rows");
   // a third of the SMs: enough stores in flight for the links, the rest stay
@@ -157,10 +112,9 @@ int peer_scatter(const PeerScatterArgs& a, cudaStream_t st) {
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "peer scatter");
 }
 
-int peer_wait(const uint32_t* flags, int nkinds, int N, int r, uint32_t epoch, uint32_t site, cudaStream_t st) {
-  if (N < 2 || N > kMaxPeers || nkinds < 1 || nkinds * kMaxPeers > 1024)
-    return set_error(LTXB_EINVAL, "peer wait: %d ranks, %d flag kinds", N, nkinds);
-  peer_wait_kernel<<<1, nkinds * kMaxPeers, 0, st>>>(flags, nkinds, N, r, epoch, site);
+int peer_wait(const uint32_t* flags, int N, int r, uint32_t epoch, uint32_t site, cudaStream_t st) {
+  if (N < 2 || N > kMaxPeers) return set_error(LTXB_EINVAL, "peer wait: %d ranks", N);
+  peer_wait_kernel<<<1, 32, 0, st>>>(flags, N, r, epoch, site);
   launched();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LTXB_OK : set_cuda_error(e, "peer wait");

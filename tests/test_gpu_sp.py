@@ -1,6 +1,6 @@
 """Multi-GPU test of the sequence-parallel block, with each of the library's
 exchanges (LTXB_SP): the head-parallel exchange by stores into the other
-ranks' memory, the same exchange over NCCL send/recv, the K/V all-gather
+ranks' memory (the default), the same exchange over NCCL send/recv, the K/V all-gather
 with split-K/V attention, and the send/recv ring:
 tokens split across ranks, each rank holding its slice of x / tidx / RoPE
 tables; the gathered outputs must match the f64 oracle of the whole block and
@@ -25,7 +25,8 @@ D, FF, S = 256, 512, 16
 
 def _worker(rank, world, uid, grid, seed, mode, algo, q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    os.environ["LTXB_SP"] = algo
+    if algo != "default":
+        os.environ["LTXB_SP"] = algo
     os.environ["LTXB_SP_RING"] = "0"
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -47,7 +48,7 @@ def _worker(rank, world, uid, grid, seed, mode, algo, q):
         part = (x[sl].contiguous(), tstab, tidx[sl].contiguous(), ctx, pts2, cos[sl].contiguous(),
                 sin[sl].contiguous())
         comm = ltxb.Comm(uid, rank, world, rank) if world > 1 else None
-        if comm is not None and algo == "peer" and not comm.peer_mapped():
+        if comm is not None and algo in ("peer", "default") and not comm.peer_mapped():
             raise RuntimeError("peer windows not mapped")
         blk = ltxb.Block(w, comm)
         out = blk.forward(*part)
@@ -68,7 +69,7 @@ def _worker(rank, world, uid, grid, seed, mode, algo, q):
         q.put((rank, None, False, -99, repr(exc)))
 
 
-def _run(world, grid, seed, mode, algo="alltoall"):
+def _run(world, grid, seed, mode, algo="default"):
     return _spawn(world, _worker, (grid, seed, mode, algo))
 
 
@@ -99,7 +100,7 @@ def _spawn(world, target, args):
     return np.concatenate([res[r][0] for r in range(world)], axis=0)
 
 
-@pytest.mark.parametrize("algo", ["peer", "alltoall", "allgather", "ring"])
+@pytest.mark.parametrize("algo", ["default", "alltoall", "allgather", "ring"])
 @pytest.mark.parametrize("mode,grid", [("bf16", (2, 4, 32)), ("int8", (3, 4, 16))])
 def test_sp_block_matches_single_gpu_and_oracle(mode, grid, algo):
     if torch.cuda.device_count() < 2:
@@ -114,7 +115,7 @@ def test_sp_block_matches_single_gpu_and_oracle(mode, grid, algo):
     assert ref.rel_rms(sp, want) < 5e-3
     assert ref.rel_rms(single, want) < 5e-3
     assert ref.rel_rms(sp, single) < 3e-3
-    if algo in ("peer", "alltoall"):  # every head computed as on one GPU
+    if algo in ("default", "alltoall"):  # every head computed as on one GPU
         assert np.array_equal(sp, single)
 
 
