@@ -117,6 +117,7 @@ struct Bufs {
   float* kv2_32 = nullptr;// [S, 2D]  f32 prompt K/V projections (tensor-core modes)
   float* x_ca = nullptr;  // [T, D]
   void* h = nullptr;      // [T, FF]
+  float* part = nullptr;  // split-K partials of the GEMMs' trailing tiles (gemm_part_floats())
   void* deq = nullptr;    // bf16: the int8 weights of one linear expanded (unfused int8 path)
   size_t deq_elems = 0;   // its capacity in elements
   float* o_acc = nullptr; // [T, D]  ring state
@@ -212,6 +213,7 @@ static size_t layout(const ltxb_weights* w, const ltxb_config* c, uint8_t* base,
   }
   b.x_ca = ws.take<float>(T * D);
   b.h = ws.take<uint8_t>(T * FF, act);
+  if (w->mode != LTXB_MODE_F32) b.part = ws.take<float>(gemm_part_floats());
   if (w->mode == LTXB_MODE_INT8 && !g_fused_dequant) {
     // the largest int8 matrix expanded at once: the fused q/k/v [3D, D], an
     // FFN one [FF, D], or the prompt K/V's (hi | lo) split [2D, 2D]
@@ -275,6 +277,7 @@ static int run_lin(const LinCall& lc, const Lin& L, const void* A, int lda, int 
   g.tk = lc.tk;
   g.ada_row = ada_row;
   g.ada_d = w->D;
+  g.part = lc.b->part;
   if (L.wq) {
     if (g_fused_dequant) {
       g.B = L.wq;
@@ -897,6 +900,8 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
       g.N = 2 * D;
       g.K = parts * D;
       g.bn = 128;  // 64 CTAs for the 128 text tokens instead of 32
+      g.part = b.part;
+      g.ksplit_all = 1;  // one M tile: its K loop, not its width, sets the time
       g.epi = EPI_F32;
       g.bias = L.b;
       g.out = b.kv2_32;

@@ -91,6 +91,106 @@ __device__ __forceinline__ uint4 dequant8(uint2 q, float s) {
   return o;
 }
 
+// Work units of a launch: tiles [0, dp) whole, then the ks_tiles trailing
+// tiles in ks pieces of their K loop each (piece i = (tile - dp) ks + s).
+struct Unit {
+  int tile, kb0, kb1, piece;  // piece < 0: a whole tile
+};
+__device__ __forceinline__ Unit unit_of(int u, int num_tiles, int nkb, const GemmArgs& a) {
+  const int dp = num_tiles - a.ks_tiles;
+  if (u < dp) return Unit{u, 0, nkb, -1};
+  const int i = u - dp, s = i % a.ks;
+  return Unit{dp + i / a.ks, (int)((long long)s * nkb / a.ks), (int)((long long)(s + 1) * nkb / a.ks), i};
+}
+
+// The fused tail of the generic epilogue for 32 accumulator columns
+// [col0, col0 + 32) of one row: bias, then the epilogue's transform and
+// store; EPI_BF16_SSQ also accumulates the row's sum of squares (in column
+// order). Shared by the GEMM and its split-K fix-up, so both produce the
+// same bits from the same accumulator values.
+template <int EPI>
+__device__ __forceinline__ void epi_chunk(const GemmArgs& args, float (&v)[32], int row, int col0, int trow,
+                                          float& ssq) {
+  if (args.bias != nullptr) {
+    const uint4* bp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(args.bias) + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 b = __ldg(bp + j);
+      v[8 * j + 0] += bf16_lo(b.x); v[8 * j + 1] += bf16_hi(b.x);
+      v[8 * j + 2] += bf16_lo(b.y); v[8 * j + 3] += bf16_hi(b.y);
+      v[8 * j + 4] += bf16_lo(b.z); v[8 * j + 5] += bf16_hi(b.z);
+      v[8 * j + 6] += bf16_lo(b.w); v[8 * j + 7] += bf16_hi(b.w);
+    }
+  }
+  if (EPI == EPI_BF16 || EPI == EPI_BF16_SSQ || EPI == EPI_GELU_BF16) {
+    if (EPI == EPI_GELU_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
+    }
+    if (EPI == EPI_BF16_SSQ) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ssq = fmaf(v[j], v[j], ssq);
+    }
+    uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 o;
+      o.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+      o.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+      o.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+      o.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+      op[j] = o;
+    }
+  } else if (EPI == EPI_RESID_F32) {
+    // out = xres + y * (sst[r] + tstab[tidx[row], r])
+    const float4* xp =
+        args.xres ? reinterpret_cast<const float4*>(args.xres + (size_t)row * args.ldx + col0) : nullptr;
+    const float4* sp = reinterpret_cast<const float4*>(args.sst + (size_t)args.ada_row * args.ada_d + col0);
+    const float4* tp =
+        reinterpret_cast<const float4*>(args.tstab + ((size_t)trow * 9 + args.ada_row) * args.ada_d + col0);
+    float4* op = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 xv = xp ? xp[j] : make_float4(0.f, 0.f, 0.f, 0.f), sv = __ldg(sp + j), tv = __ldg(tp + j), o;
+      o.x = xv.x + v[4 * j + 0] * (tv.x + sv.x);
+      o.y = xv.y + v[4 * j + 1] * (tv.y + sv.y);
+      o.z = xv.z + v[4 * j + 2] * (tv.z + sv.z);
+      o.w = xv.w + v[4 * j + 3] * (tv.w + sv.w);
+      op[j] = o;
+    }
+  } else {  // EPI_F32 / EPI_GATE2SIG_F32
+    float4* op = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      if (EPI == EPI_GATE2SIG_F32) {
+        o.x = 2.0f / (1.0f + __expf(-o.x));
+        o.y = 2.0f / (1.0f + __expf(-o.y));
+        o.z = 2.0f / (1.0f + __expf(-o.z));
+        o.w = 2.0f / (1.0f + __expf(-o.w));
+      }
+      op[j] = o;
+    }
+  }
+}
+
+// A split piece's accumulator rows, raw, into its [128 x BN] f32 partial.
+template <int BN>
+__device__ __forceinline__ void dump_partial(const GemmArgs& args, uint32_t tbase, int piece, int row_local) {
+  float* dst = args.part + ((size_t)piece * GEMM_BM + row_local) * BN;
+#pragma unroll 1
+  for (int cc = 0; cc < BN / 32; ++cc) {
+    uint32_t r[32];
+    tmem_ld32(tbase + cc * 32, r);
+    tmem_wait_ld();
+    float4* d4 = reinterpret_cast<float4*>(dst + cc * 32);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      d4[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                          __uint_as_float(r[4 * j + 3]));
+  }
+}
+
 template <int BN, bool BQ8, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -118,6 +218,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
   const int M = args.M, N = args.N, K = args.K;
   const int num_m = (M + GEMM_BM - 1) / GEMM_BM, num_n = N / BN, nkb = K / GEMM_BK;
   const int num_tiles = num_m * num_n;
+  const int num_units = num_tiles - args.ks_tiles + args.ks_tiles * args.ks;
+  const int dp = num_tiles - args.ks_tiles;  // units below dp are whole tiles
   const int kw = args.b_kwrap > 0 ? args.b_kwrap : K;  // B's own K (columns repeat with this period)
 
   if (threadIdx.x == 0) {
@@ -153,10 +255,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       const uint32_t bytes = C::A_BYTES + (BQ8 ? C::BQ_BYTES : C::B_BYTES);
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+        const Unit un = unit_of(u, num_tiles, nkb, args);
         int m, n;
-        tile_coords(tile, num_m, num_n, m, n);
-        for (int kb = 0; kb < nkb; ++kb) {
+        tile_coords(un.tile, num_m, num_n, m, n);
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, 0x101)) goto done;
           mbar_arrive_expect_tx(&full[s], bytes);
           tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * GEMM_BK, m * GEMM_BM);
@@ -176,20 +279,21 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
+        const Unit un = unit_of(u, num_tiles, nkb, args);
         const int acc = it & 1;
         const uint32_t aph = (it >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aph ^ 1, 0x102)) goto done;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(BQ8 ? &deq[s] : &full[s], ph, 0x103)) goto done;
           tc_fence_after();
           const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + s * C::A_BYTES));
           const uint64_t db = sdesc_kmajor_sw128(smem_u32(sB + s * C::B_BYTES));
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k)
-            umma_ss(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+            umma_ss(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb != un.kb0 || k != 0));
           umma_commit(&empty[s]);
           if (++s == S) { s = 0; ph ^= 1; }
         }
@@ -218,17 +322,26 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
       tma_load_2d(xbuf + b * C::XCHUNK, &tmX, &xfull[b], n * BN + cc * 32, m * GEMM_BM);
       ++issued;
     };
-    if (leader && (int)blockIdx.x < num_tiles) load_chunk(blockIdx.x, 0);
+    if (leader && (int)blockIdx.x < dp) load_chunk(blockIdx.x, 0);
     int it = 0;
     bool failed = false;
-    for (int tile = blockIdx.x; tile < num_tiles && !failed; tile += gridDim.x, ++it) {
-      int m, n;
-      tile_coords(tile, num_m, num_n, m, n);
+    for (int u = blockIdx.x; u < num_units && !failed; u += gridDim.x, ++it) {
+      const int tile = u;  // whole tiles come first (u < dp)
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
       const bool tok = warp_wait(&tfull[acc], aph, 0x104);
       if (named_bar_any(1, 128, !tok)) break;
       tc_fence_after();
+      if (u >= dp) {  // a split piece: its raw partial, the fix-up kernel applies the epilogue
+        const Unit un = unit_of(u, num_tiles, nkb, args);
+        dump_partial<BN>(args, tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN, un.piece, row_local);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
+      }
+      int m, n;
+      tile_coords(tile, num_m, num_n, m, n);
       const int row = m * GEMM_BM + row_local;
       const int trow = row < M ? table_row(args.tidx, row, args.tk) : 0;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
@@ -280,7 +393,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
           tma_store_2d(&tmO, xbuf + b * C::XCHUNK, col0, m * GEMM_BM);
           bulk_commit();
           const int ntile = cc + 1 < NCH ? tile : tile + (int)gridDim.x;
-          if (ntile < num_tiles) {
+          if (ntile < dp) {
             bulk_wait_read<1>();  // the store that last read the other buffer is done with it
             load_chunk(ntile, cc + 1 < NCH ? cc + 1 : 0);
           }
@@ -302,94 +415,35 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_local = q * 32 + lane;
     int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
-      int m, n;
-      tile_coords(tile, num_m, num_n, m, n);
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
+      const Unit un = unit_of(u, num_tiles, nkb, args);
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
       if (!warp_wait(&tfull[acc], aph, 0x104)) break;
       tc_fence_after();
-      const int row = m * GEMM_BM + row_local;
-      const bool row_ok = row < M;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      float ssq = 0.f;
-      int trow = 0;
-      if (EPI == EPI_RESID_F32 && row_ok) trow = table_row(args.tidx, row, args.tk);
+      if (un.piece >= 0) {  // a split piece: its raw partial, the fix-up kernel applies the epilogue
+        dump_partial<BN>(args, tbase, un.piece, row_local);
+      } else {
+        int m, n;
+        tile_coords(un.tile, num_m, num_n, m, n);
+        const int row = m * GEMM_BM + row_local;
+        const bool row_ok = row < M;
+        float ssq = 0.f;
+        const int trow = (EPI == EPI_RESID_F32 && row_ok) ? table_row(args.tidx, row, args.tk) : 0;
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        uint32_t r[32];
-        tmem_ld32(tbase + cc * 32, r);
-        tmem_wait_ld();
-        const int col0 = n * BN + cc * 32;
-        float v[32];
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tbase + cc * 32, r);
+          tmem_wait_ld();
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (args.bias != nullptr) {
-          const uint4* bp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(args.bias) + col0);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 b = __ldg(bp + j);
-            v[8 * j + 0] += bf16_lo(b.x); v[8 * j + 1] += bf16_hi(b.x);
-            v[8 * j + 2] += bf16_lo(b.y); v[8 * j + 3] += bf16_hi(b.y);
-            v[8 * j + 4] += bf16_lo(b.z); v[8 * j + 5] += bf16_hi(b.z);
-            v[8 * j + 6] += bf16_lo(b.w); v[8 * j + 7] += bf16_hi(b.w);
-          }
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (row_ok) epi_chunk<EPI>(args, v, row, n * BN + cc * 32, trow, ssq);
         }
-        if (!row_ok) continue;
-        if (EPI == EPI_BF16 || EPI == EPI_BF16_SSQ || EPI == EPI_GELU_BF16) {
-          if (EPI == EPI_GELU_BF16) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
-          }
-          if (EPI == EPI_BF16_SSQ) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) ssq = fmaf(v[j], v[j], ssq);
-          }
-          uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) +
-                                               (size_t)row * args.ldo + col0);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 o;
-            o.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
-            o.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-            o.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-            o.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-            op[j] = o;
-          }
-        } else if (EPI == EPI_RESID_F32) {
-          // out = xres + y * (sst[r] + tstab[tidx[row], r])
-          const float4* xp =
-              args.xres ? reinterpret_cast<const float4*>(args.xres + (size_t)row * args.ldx + col0) : nullptr;
-          const float4* sp = reinterpret_cast<const float4*>(args.sst + (size_t)args.ada_row * args.ada_d + col0);
-          const float4* tp = reinterpret_cast<const float4*>(
-              args.tstab + ((size_t)trow * 9 + args.ada_row) * args.ada_d + col0);
-          float4* op = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + col0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 xv = xp ? xp[j] : make_float4(0.f, 0.f, 0.f, 0.f), sv = __ldg(sp + j), tv = __ldg(tp + j), o;
-            o.x = xv.x + v[4 * j + 0] * (tv.x + sv.x);
-            o.y = xv.y + v[4 * j + 1] * (tv.y + sv.y);
-            o.z = xv.z + v[4 * j + 2] * (tv.z + sv.z);
-            o.w = xv.w + v[4 * j + 3] * (tv.w + sv.w);
-            op[j] = o;
-          }
-        } else {  // EPI_F32 / EPI_GATE2SIG_F32
-          float4* op = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + col0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            if (EPI == EPI_GATE2SIG_F32) {
-              o.x = 2.0f / (1.0f + __expf(-o.x));
-              o.y = 2.0f / (1.0f + __expf(-o.y));
-              o.z = 2.0f / (1.0f + __expf(-o.z));
-              o.w = 2.0f / (1.0f + __expf(-o.w));
-            }
-            op[j] = o;
-          }
-        }
+        if (EPI == EPI_BF16_SSQ && row_ok && n * BN < args.ssq_cols)
+          args.ssq[(size_t)row * args.ssq_ld + n] = ssq;
       }
-      if (EPI == EPI_BF16_SSQ && row_ok && n * BN < args.ssq_cols)
-        args.ssq[(size_t)row * args.ssq_ld + n] = ssq;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -400,10 +454,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, BQ8>::NUM_THREADS, 1)
     int s = 0;
     uint32_t ph = 0;
     const int ngroups = kw / 128;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      const Unit un = unit_of(u, num_tiles, nkb, args);
       int m, n;
-      tile_coords(tile, num_m, num_n, m, n);
-      for (int kb = 0; kb < nkb; ++kb) {
+      tile_coords(un.tile, num_m, num_n, m, n);
+      for (int kb = un.kb0; kb < un.kb1; ++kb) {
         if (!warp_wait(&full[s], ph, 0x105)) goto done;
         const uint8_t* src = sBq + s * C::BQ_BYTES;
         uint8_t* dst = sB + s * C::B_BYTES;
@@ -435,9 +490,70 @@ done:
   }
 }
 
+// Split-K fix-up: one CTA per (split tile, group of 32 rows), one warp per
+// 32-column chunk, one thread per row: sums the tile's ks partials in piece
+// order (so the result does not depend on which CTA ran which piece) and
+// applies the whole-tile path's epilogue. The sum of squares of a row
+// (EPI_BF16_SSQ) adds the chunks' sums in chunk order.
+constexpr int FIX_ROWS = 32;
+template <int BN, int EPI>
+__global__ void __launch_bounds__(FIX_ROWS * (BN / 32)) gemm_fixup_kernel(const GemmArgs args) {
+  __shared__ float red[BN / 32][FIX_ROWS];
+  const int num_m = (args.M + GEMM_BM - 1) / GEMM_BM, num_n = args.N / BN;
+  const int groups = GEMM_BM / FIX_ROWS;
+  const int ti = blockIdx.x / groups, rg = blockIdx.x % groups;
+  const int tile = num_m * num_n - args.ks_tiles + ti;
+  int m, n;
+  tile_coords(tile, num_m, num_n, m, n);
+  const int rl = rg * FIX_ROWS + (threadIdx.x % FIX_ROWS), cc = threadIdx.x / FIX_ROWS;
+  const int row = m * GEMM_BM + rl;
+  const bool row_ok = row < args.M;
+  float ssq = 0.f;
+  if (row_ok) {
+    const int trow = EPI == EPI_RESID_F32 ? table_row(args.tidx, row, args.tk) : 0;
+    const float4* src = reinterpret_cast<const float4*>(
+        args.part + ((size_t)ti * args.ks * GEMM_BM + rl) * BN + cc * 32);
+    const size_t pstride = (size_t)GEMM_BM * BN / 4;  // float4 between consecutive pieces
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 a = src[j];
+      v[4 * j] = a.x;
+      v[4 * j + 1] = a.y;
+      v[4 * j + 2] = a.z;
+      v[4 * j + 3] = a.w;
+    }
+    for (int s = 1; s < args.ks; ++s) {
+      float4 a[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = src[s * pstride + j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[4 * j] += a[j].x;
+        v[4 * j + 1] += a[j].y;
+        v[4 * j + 2] += a[j].z;
+        v[4 * j + 3] += a[j].w;
+      }
+    }
+    epi_chunk<EPI>(args, v, row, n * BN + cc * 32, trow, ssq);
+  }
+  if (EPI == EPI_BF16_SSQ) {
+    red[cc][threadIdx.x % FIX_ROWS] = ssq;
+    __syncthreads();
+    if (cc == 0 && row_ok && n * BN < args.ssq_cols) {
+      float t = red[0][threadIdx.x];
+#pragma unroll
+      for (int c = 1; c < BN / 32; ++c) t += red[c][threadIdx.x];
+      args.ssq[(size_t)row * args.ssq_ld + n] = t;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+
+size_t gemm_part_floats() { return (size_t)sm_count() * GEMM_BM * 256; }
 
 template <int BN, bool BQ8, int EPI>
 static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx, const CUtensorMap& to,
@@ -456,12 +572,43 @@ static int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtens
     attr_set[dev].store(true, std::memory_order_release);
   }
   const int num_tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * (a.N / BN);
-  const int grid = num_tiles < sm_count() ? num_tiles : sm_count();
+  const int num_units = num_tiles - a.ks_tiles + a.ks_tiles * a.ks;
+  const int grid = num_units < sm_count() ? num_units : sm_count();
   kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, tx, to, a);
   launched();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "gemm launch");
+  if (a.ks_tiles > 0) {
+    gemm_fixup_kernel<BN, EPI><<<a.ks_tiles * (GEMM_BM / FIX_ROWS), FIX_ROWS * (BN / 32), 0, st>>>(a);
+    launched();
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error(e, "gemm split-K fix-up launch");
+  }
   return LTXB_OK;
+}
+
+// Which tiles to split (see GemmArgs::part): the tiles of a last wave that
+// would fill at most a quarter of the SMs (or every tile with ksplit_all),
+// each into as many K pieces as fill the SMs, at most 8 and at least 2
+// K blocks of 64 per piece. Sets a.ks_tiles / a.ks (0 / 1: no split).
+static void plan_split(GemmArgs& a, int bn) {
+  a.ks_tiles = 0;
+  a.ks = 1;
+  if (!a.part || a.b_int8) return;
+  const int P = sm_count(), nkb = a.K / GEMM_BK;
+  const int tiles = ((a.M + GEMM_BM - 1) / GEMM_BM) * (a.N / bn);
+  int r = 0;
+  if (a.ksplit_all)
+    r = tiles;
+  else if (tiles > P && tiles % P != 0 && (tiles % P) * 4 <= P)
+    r = tiles % P;
+  if (r == 0 || r > P) return;
+  int ks = P / r;
+  if (ks > 8) ks = 8;
+  if (ks > nkb / 2) ks = nkb / 2;
+  if (ks < 2) return;
+  a.ks_tiles = r;
+  a.ks = ks;
 }
 
 template <int BN, bool BQ8>
@@ -494,15 +641,17 @@ int gemm_check(const GemmArgs& a, int* bn_out) {
     return set_error(LTXB_EINVAL, "gemm: operands must be 16-byte aligned with 16-byte row strides");
   // the epilogue moves 16-byte vectors of out, bias and the residual input
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  if (!a16(a.out) || !a16(a.bias) || !a16(a.xres) || (a.xres && a.ldx % 4))
+  if (!a16(a.out) || !a16(a.bias) || !a16(a.xres) || !a16(a.part) || (a.xres && a.ldx % 4))
     return set_error(LTXB_EINVAL, "gemm: out, bias and residual must be 16-byte aligned");
   if (bn_out) *bn_out = bn;
   return LTXB_OK;
 }
 
-int gemm_tc(const GemmArgs& a, cudaStream_t st) {
+int gemm_tc(const GemmArgs& a_in, cudaStream_t st) {
   int bn = 0;
-  if (int rc = gemm_check(a, &bn)) return rc;
+  if (int rc = gemm_check(a_in, &bn)) return rc;
+  GemmArgs a = a_in;
+  plan_split(a, bn);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda, GEMM_BK, GEMM_BM,
                         CU_TENSOR_MAP_SWIZZLE_128B);

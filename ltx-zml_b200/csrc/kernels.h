@@ -80,7 +80,18 @@ struct GemmArgs {
   // split-precision products (the f32-exact prompt K/V): B's columns repeat
   // with period b_kwrap (its real K; 0 = no repeat)
   int b_kwrap;
+  // split-K of trailing tiles (deterministic): with `part` set (f32 scratch
+  // of gemm_part_floats() floats), gemm_tc splits the K loop of the tiles
+  // of a last wave that would leave most SMs idle (or of every tile with
+  // ksplit_all) into pieces that write f32 partials, and a fix-up kernel sums
+  // them in a fixed order and applies the epilogue. ks_tiles / ks are set
+  // by gemm_tc (the split tiles, pieces per tile).
+  float* part;
+  int ksplit_all;
+  int ks_tiles, ks;
 };
+// floats of split-K scratch gemm_tc may use (one [128 x 256] tile per SM)
+size_t gemm_part_floats();
 // Shape, alignment and tile checks of gemm_tc, on the host, launching
 // nothing; *bn_out receives the N tile gemm_tc will use.
 int gemm_check(const GemmArgs& a, int* bn_out);

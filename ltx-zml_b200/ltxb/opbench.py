@@ -4,7 +4,7 @@ timing and for sizing profiler captures:
     PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench attention --T 8192 --H 8 --reps 3
     PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench dq_gemm --M 8192 --N 4096 --K 4096 [--unfused]
     PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench gemm --M 8192 --N 4096 --K 4096
-    PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench block --T 8192 --reps 3
+    PYTHONPATH=ltx-zml_b200 python -m ltxb.opbench block --T 8192 --reps 3 [--phases]
 
 `block` runs whole int8 blocks (BASELINE config-3 architecture: D 4096,
 32 x 128 heads, FFN 16384, S 128, int8 g128 EXT weights with bf16 scales)
@@ -22,7 +22,7 @@ import argparse
 
 import torch
 
-from . import attention, dq_gemm, gemm_bf16, device_status
+from . import attention, dq_gemm, gemm_bf16, device_status, profile_collect, profile_enable
 
 
 def _time(fn, reps: int) -> float:
@@ -48,6 +48,7 @@ def main(argv=None) -> int:
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--unfused", action="store_true")
     ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--phases", action="store_true", help="block: also print the per-phase device times")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(0)
@@ -69,6 +70,13 @@ def main(argv=None) -> int:
         T, D, S, FF = a.T, 4096, 128, 16384
         flop = 12 * T * D * D + 4 * S * D * D + 4 * T * D * 32 + 4 * T * D * FF + 4 * T * T * D + 4 * T * S * D
         print(f"block T={a.T}: {ms:.4f} ms/block {flop / ms / 1e9:.1f} TFLOP/s status={device_status()}")
+        if a.phases:  # the library's per-phase device times over the same calls
+            profile_collect(reset=True)
+            profile_enable(True)
+            _time(lambda: blk.forward(x, tstab, tidx, ctx, pts2, cos, sin, out=out), a.reps)
+            profile_enable(False)
+            ph = profile_collect(reset=True)
+            print("phases (ms per block): " + " ".join(f"{k}={v[0] / max(v[2], 1):.4f}" for k, v in ph.items()))
         w.free()
         return 0
     if a.op == "attention":
