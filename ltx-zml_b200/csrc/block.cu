@@ -900,8 +900,11 @@ static int run_block(const ltxb_weights* w, const ltxb_block_io* io, const ltxb_
       g.N = 2 * D;
       g.K = parts * D;
       g.bn = 128;  // 64 CTAs for the 128 text tokens instead of 32
+      // one M tile: its K loop, not its width, sets the time, so it is split
+      // in K -- except under the peer exchange, whose scatter shares the SMs
+      // with it then (8 GPUs: 0.197 ms unsplit, 0.229 ms split)
       g.part = b.part;
-      g.ksplit_all = 1;  // one M tile: its K loop, not its width, sets the time
+      g.ksplit_all = !(sp && alg == SP_PEER);
       g.epi = EPI_F32;
       g.bias = L.b;
       g.out = b.kv2_32;
