@@ -540,7 +540,9 @@ def ring_step(rank: int, nranks: int, step: int) -> dict:
 
 
 class Comm:
-    """NCCL communicator for the ring of K/V shards (one rank per GPU)."""
+    """Sequence-parallel group (one rank per GPU): an NCCL communicator plus,
+    with 2..8 ranks in separate processes, every rank's peer-memory window
+    mapped in every other rank (the default head-parallel exchange)."""
 
     @staticmethod
     def unique_id() -> bytes:
