@@ -105,6 +105,8 @@ def test_null_arguments_rejected():
     assert ltxb.lib.ltxb_weights_upload(0, None, 0, None, 0, 0, 0, 0, 4096, 16384, ctypes.byref(h)) == ltxb.EINVAL
     ltxb.lib.ltxb_weights_free(None)
     ltxb.lib.ltxb_comm_free(None)
+    ltxb.lib.ltxb_comm_abort(None)
+    assert ltxb.lib.ltxb_comm_peer_mapped(None) == 0  # no communicator: no peer windows
 
 
 def test_blob_writer_matches_reference_packer():
