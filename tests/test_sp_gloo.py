@@ -1,9 +1,13 @@
 """CPU tests of the sequence-parallel host logic with real multi-process ranks
 over gloo:
 
-* the default path: each rank all-gathers the K/V shards, splits the
-  gathered K/V range and merges the per-split (m, l, O) partials the way the
-  combine kernel does; the result must equal dense attention;
+* the head-parallel exchange (the library's default, by stores into the
+  other ranks' memory, or over NCCL with LTXB_SP=alltoall): q/k/v blocks to
+  the ranks owning their heads, attention over all tokens of the owned
+  heads, output rows back to the ranks holding their tokens;
+* the all-gather alternative: each rank all-gathers the K/V shards, splits
+  the gathered K/V range and merges the per-split (m, l, O) partials the way
+  the combine kernel does; the result must equal dense attention;
 * the ring alternative: the library's ring schedule (ltxb_ring_step, the
   function the block's NCCL ring follows) drives a K/V shard exchange and
   each rank merges per-shard partials;
